@@ -1,0 +1,444 @@
+// d3s_capi.cu - the C ABI declared in include/d3s.h: keys, contexts, argument
+// checks, and the entry points that mirror drama3-mlx's sampling interface
+// (src/model.h:169-176, src/testapi.c:155-166). No entry point exits the
+// process; errors come back as D3S_ERR_* codes with a message.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "d3s.h"
+#include "d3s_device.cuh"
+#include "d3s_kernels.cuh"
+
+struct d3s_ctx {
+  int device = 0;
+  d3s::Scratch scratch;
+  // staging for the host-pointer entry point (d3_sample)
+  float *h_logits_dev = nullptr;
+  int32_t *ids_dev = nullptr;
+  int32_t *status_dev = nullptr;
+  size_t logits_cap = 0;  // floats
+  size_t rows_cap = 0;
+  cudaStream_t stream = nullptr;
+};
+
+namespace {
+
+thread_local std::string g_err;
+thread_local int g_last_status = D3S_OK;
+std::mutex g_key_mu;
+d3s_key g_key = {{0u, 0u}};  // the library's global key (MLX seeds its own from time)
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(D3S_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int reserve_scratch(d3s_ctx *ctx, int64_t rows) {
+  if (ctx->scratch.capacity >= rows) return D3S_OK;
+  int64_t cap = std::max<int64_t>(rows, 1024);
+  int32_t *d = nullptr;
+  uint32_t *c = nullptr;
+  cudaError_t e = cudaMalloc(&d, (size_t)cap * sizeof(int32_t));
+  if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e));
+  if (!ctx->scratch.counters) {
+    e = cudaMalloc(&c, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c, 0, 2 * sizeof(uint32_t));
+    if (e != cudaSuccess) {
+      cudaFree(d);
+      if (c) cudaFree(c);
+      return fail(D3S_ERR_NOMEM, "scratch counters: %s", cudaGetErrorString(e));
+    }
+    ctx->scratch.counters = c;
+  }
+  if (ctx->scratch.deferred) {
+    cudaDeviceSynchronize();  // the old list may be in use by queued work
+    cudaFree(ctx->scratch.deferred);
+  }
+  ctx->scratch.deferred = d;
+  ctx->scratch.capacity = cap;
+  return D3S_OK;
+}
+
+int check_request(const d3s_request *r) {
+  if (!r) return fail(D3S_ERR_ARG, "null request");
+  if (r->N < 0 || r->V < 1) return fail(D3S_ERR_ARG, "bad shape N=%d V=%d", r->N, r->V);
+  if (r->V > D3S_MAX_V) return fail(D3S_ERR_UNSUPPORTED, "V=%d exceeds %d", r->V, D3S_MAX_V);
+  if (r->dtype != D3S_F32 && r->dtype != D3S_BF16) return fail(D3S_ERR_ARG, "bad dtype %d", r->dtype);
+  if (r->ld < r->V) return fail(D3S_ERR_ARG, "ld=%lld < V=%d", (long long)r->ld, r->V);
+  if (r->N > 0 && (!r->logits || !r->ids)) return fail(D3S_ERR_ARG, "null logits or ids");
+  if (!r->top_k_rows) {
+    if (r->top_k < 1) return fail(D3S_ERR_ARG, "top_k=%d < 1", r->top_k);
+    if (std::min(r->top_k, r->V) > D3S_MAX_K)
+      return fail(D3S_ERR_UNSUPPORTED, "k=%d exceeds %d", std::min(r->top_k, r->V), D3S_MAX_K);
+  }
+  if (!r->temperature_rows && r->temperature != r->temperature)
+    return fail(D3S_ERR_ARG, "temperature is NaN");
+  switch (r->noise) {
+    case D3S_NOISE_KEY: {
+      if (r->top_k_rows) return fail(D3S_ERR_ARG, "one-key noise needs one top_k for the batch");
+      const uint64_t words = (uint64_t)r->N * (uint64_t)std::min(r->top_k, r->V);
+      if (words >= (1ull << 32)) return fail(D3S_ERR_UNSUPPORTED, "N*k >= 2^32 uniform words");
+      break;
+    }
+    case D3S_NOISE_SEEDS:
+      if (r->N > 0 && !r->seeds) return fail(D3S_ERR_ARG, "null seeds");
+      break;
+    case D3S_NOISE_GIVEN:
+      if (r->N > 0 && !r->u) return fail(D3S_ERR_ARG, "null u");
+      if (r->top_k_rows) return fail(D3S_ERR_ARG, "given noise needs one top_k for the batch");
+      if (r->ld_u < std::min(r->top_k, r->V)) return fail(D3S_ERR_ARG, "ld_u < k");
+      break;
+    default:
+      return fail(D3S_ERR_ARG, "bad noise mode %d", r->noise);
+  }
+  if ((r->probs || r->topk_ids)) {
+    const int kmax = r->top_k_rows ? D3S_MAX_K : std::min(r->top_k, r->V);
+    if (r->ld_out < std::min(kmax, r->V)) return fail(D3S_ERR_ARG, "ld_out too small");
+  }
+  return D3S_OK;
+}
+
+d3s::KArgs to_kargs(const d3s_request *r, const d3s_ctx *ctx) {
+  d3s::KArgs a{};
+  a.logits = r->logits;
+  a.ld = r->ld;
+  a.dtype = r->dtype;
+  a.N = r->N;
+  a.V = r->V;
+  a.T = r->temperature;
+  a.top_p = r->top_p;
+  a.top_k = r->top_k;
+  a.T_rows = r->temperature_rows;
+  a.p_rows = r->top_p_rows;
+  a.k_rows = r->top_k_rows;
+  a.noise = r->noise;
+  a.key = make_uint2(r->key.k[0], r->key.k[1]);
+  a.seeds = r->seeds;
+  a.u = r->u;
+  a.ld_u = r->ld_u;
+  a.ids = r->ids;
+  a.status = r->status;
+  a.kept = r->kept;
+  a.probs = r->probs;
+  a.topk_ids = r->topk_ids;
+  a.ld_out = r->ld_out;
+  a.deferred = ctx->scratch.deferred;
+  a.deferred_n = ctx->scratch.counters;
+  a.wide_done = ctx->scratch.counters ? ctx->scratch.counters + 1 : nullptr;
+  return a;
+}
+
+int next_key_locked(d3s_key *state, d3s_key *sub) {
+  uint2 k0, k1;
+  d3s::key_split(make_uint2(state->k[0], state->k[1]), k0, k1);
+  state->k[0] = k0.x;
+  state->k[1] = k0.y;
+  sub->k[0] = k1.x;
+  sub->k[1] = k1.y;
+  return D3S_OK;
+}
+
+int take_subkey(d3s_key *state, d3s_key *sub) {
+  if (state) return next_key_locked(state, sub);
+  std::lock_guard<std::mutex> lk(g_key_mu);
+  return next_key_locked(&g_key, sub);
+}
+
+}  // namespace
+
+extern "C" {
+
+int d3s_version(void) { return D3S_VERSION; }
+
+const char *d3s_last_error(void) { return g_err.c_str(); }
+
+int d3s_key_from_seed(uint64_t seed, d3s_key *out) {
+  if (!out) return fail(D3S_ERR_ARG, "null key");
+  const uint2 k = d3s::key_from_seed(seed);
+  out->k[0] = k.x;
+  out->k[1] = k.y;
+  return D3S_OK;
+}
+
+int d3s_key_split(const d3s_key *key, d3s_key *k0, d3s_key *k1) {
+  if (!key || !k0 || !k1) return fail(D3S_ERR_ARG, "null key");
+  uint2 a, b;
+  d3s::key_split(make_uint2(key->k[0], key->k[1]), a, b);
+  k0->k[0] = a.x;
+  k0->k[1] = a.y;
+  k1->k[0] = b.x;
+  k1->k[1] = b.y;
+  return D3S_OK;
+}
+
+int d3s_seed(d3s_key *state, uint64_t seed) {
+  const uint2 k = d3s::key_from_seed(seed);
+  if (state) {
+    state->k[0] = k.x;
+    state->k[1] = k.y;
+    return D3S_OK;
+  }
+  std::lock_guard<std::mutex> lk(g_key_mu);
+  g_key.k[0] = k.x;
+  g_key.k[1] = k.y;
+  return D3S_OK;
+}
+
+int d3s_next_key(d3s_key *state, d3s_key *sub) {
+  if (!sub) return fail(D3S_ERR_ARG, "null subkey");
+  return take_subkey(state, sub);
+}
+
+int d3s_ctx_create(int device, d3s_ctx **out) {
+  if (!out) return fail(D3S_ERR_ARG, "null out");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(D3S_ERR_ARG, "device %d of %d", device, n);
+  DeviceGuard g(device);
+  if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  d3s_ctx *c = new d3s_ctx();
+  c->device = device;
+  int rc = reserve_scratch(c, 1024);
+  if (rc != D3S_OK) {
+    delete c;
+    return rc;
+  }
+  *out = c;
+  return D3S_OK;
+}
+
+int d3s_ctx_reserve(d3s_ctx *ctx, int64_t max_rows) {
+  if (!ctx || max_rows < 0) return fail(D3S_ERR_ARG, "bad ctx / rows");
+  DeviceGuard g(ctx->device);
+  return reserve_scratch(ctx, max_rows);
+}
+
+void d3s_ctx_destroy(d3s_ctx *ctx) {
+  if (!ctx) return;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  cudaFree(ctx->scratch.deferred);
+  cudaFree(ctx->scratch.counters);
+  cudaFree(ctx->h_logits_dev);
+  cudaFree(ctx->ids_dev);
+  cudaFree(ctx->status_dev);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int d3s_sample(d3s_ctx *ctx, const d3s_request *req, void *stream) {
+  if (!ctx) return fail(D3S_ERR_ARG, "null ctx");
+  int rc = check_request(req);
+  if (rc != D3S_OK) return rc;
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  if (req->top_k_rows) {
+    rc = reserve_scratch(ctx, req->N);
+    if (rc != D3S_OK) return rc;
+  }
+  const d3s::KArgs a = to_kargs(req, ctx);
+  rc = d3s::launch_sample(a, ctx->scratch, (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "sampler launch");
+  return D3S_OK;
+}
+
+int d3s_sample_noise(d3s_ctx *ctx, d3s_key *state, int rows, int V, int top_k, float *u_dev,
+                     void *stream) {
+  if (!ctx) return fail(D3S_ERR_ARG, "null ctx");
+  if (rows < 0 || V < 1 || top_k < 1) return fail(D3S_ERR_ARG, "bad rows/V/top_k");
+  if (rows > 0 && !u_dev) return fail(D3S_ERR_ARG, "null u");
+  const int k = std::min(top_k, V);
+  if ((uint64_t)rows * (uint64_t)k >= (1ull << 32))
+    return fail(D3S_ERR_UNSUPPORTED, "rows*k >= 2^32 uniform words");
+  d3s_key sub;
+  take_subkey(state, &sub);
+  DeviceGuard g(ctx->device);
+  const int rc = d3s::launch_uniform(make_uint2(sub.k[0], sub.k[1]), rows, k, u_dev,
+                                     (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "uniform launch");
+  return D3S_OK;
+}
+
+int d3s_sample_with_noise(d3s_ctx *ctx, const void *logits_dev, int dtype, int N, int V,
+                          int64_t ld, const float *u_dev, int k, int64_t ld_u, float temperature,
+                          float top_p, int32_t *ids_dev, void *stream) {
+  if (k < 1 || k > V) return fail(D3S_ERR_ARG, "k=%d must be in [1, V=%d]", k, V);
+  d3s_request r{};
+  r.logits = logits_dev;
+  r.dtype = dtype;
+  r.N = N;
+  r.V = V;
+  r.ld = ld;
+  r.temperature = temperature;
+  r.top_p = top_p;
+  r.top_k = k;
+  r.noise = D3S_NOISE_GIVEN;
+  r.u = u_dev;
+  r.ld_u = ld_u;
+  r.ids = ids_dev;
+  return d3s_sample(ctx, &r, stream);
+}
+
+int d3s_sample_top_k_top_p(d3s_ctx *ctx, const void *logits_dev, int dtype, int N, int V,
+                           int64_t ld, float temperature, int top_k, float top_p, d3s_key *state,
+                           int32_t *ids_dev, void *stream) {
+  d3s_request r{};
+  r.logits = logits_dev;
+  r.dtype = dtype;
+  r.N = N;
+  r.V = V;
+  r.ld = ld;
+  r.temperature = temperature;
+  r.top_p = top_p;
+  r.top_k = top_k;
+  r.noise = D3S_NOISE_KEY;
+  r.ids = ids_dev;
+  int rc = check_request(&r);
+  if (rc != D3S_OK) return rc;
+  d3s_key sub;
+  take_subkey(state, &sub);  // the key advances only for a valid call
+  r.key = sub;
+  return d3s_sample(ctx, &r, stream);
+}
+
+int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
+                   void *stream) {
+  if (!ctx || op < 0 || op > 2 || n < 0) return fail(D3S_ERR_ARG, "bad math args");
+  DeviceGuard g(ctx->device);
+  const int rc = d3s::launch_math(op, x_dev, y_dev, n, (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "math launch");
+  return D3S_OK;
+}
+
+// ---- the test ABI of the reference ----
+
+static std::mutex g_default_mu;
+static d3s_ctx *g_default_ctx = nullptr;
+
+static int default_ctx(d3s_ctx **out) {
+  std::lock_guard<std::mutex> lk(g_default_mu);
+  if (!g_default_ctx) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    int rc = d3s_ctx_create(dev, &g_default_ctx);
+    if (rc != D3S_OK) return rc;
+  }
+  *out = g_default_ctx;
+  return D3S_OK;
+}
+
+static int d3_sample_impl(const float *logits, int N, int V, float temperature, int top_k,
+                          float top_p, unsigned long long seed, int *out) {
+  if (N < 0 || V < 1 || (N > 0 && (!logits || !out))) return fail(D3S_ERR_ARG, "bad d3_sample args");
+  d3s_ctx *ctx = nullptr;
+  int rc = default_ctx(&ctx);
+  if (rc != D3S_OK) return rc;
+  std::lock_guard<std::mutex> lk(g_default_mu);
+  DeviceGuard g(ctx->device);
+  cudaError_t e;
+  if (!ctx->stream) {
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+  }
+  const size_t nl = (size_t)N * (size_t)V;
+  if (nl > ctx->logits_cap) {
+    cudaFree(ctx->h_logits_dev);
+    ctx->h_logits_dev = nullptr;
+    ctx->logits_cap = 0;
+    e = cudaMalloc(&ctx->h_logits_dev, nl * sizeof(float));
+    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "logits staging: %s", cudaGetErrorString(e));
+    ctx->logits_cap = nl;
+  }
+  if ((size_t)N > ctx->rows_cap) {
+    cudaFree(ctx->ids_dev);
+    cudaFree(ctx->status_dev);
+    ctx->ids_dev = nullptr;
+    ctx->status_dev = nullptr;
+    ctx->rows_cap = 0;
+    e = cudaMalloc(&ctx->ids_dev, (size_t)N * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->status_dev, (size_t)N * sizeof(int32_t));
+    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "ids staging: %s", cudaGetErrorString(e));
+    ctx->rows_cap = (size_t)N;
+  }
+  if (N == 0) return D3S_OK;
+  d3s_seed(nullptr, seed);  // m_seed(seed), src/testapi.c:159
+  e = cudaMemcpyAsync(ctx->h_logits_dev, logits, nl * sizeof(float), cudaMemcpyHostToDevice,
+                      ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "logits upload");
+  d3s_request r{};
+  r.logits = ctx->h_logits_dev;
+  r.dtype = D3S_F32;
+  r.N = N;
+  r.V = V;
+  r.ld = V;
+  r.temperature = temperature;
+  r.top_p = top_p;
+  r.top_k = top_k;
+  r.noise = D3S_NOISE_KEY;
+  r.ids = ctx->ids_dev;
+  r.status = ctx->status_dev;
+  rc = check_request(&r);
+  if (rc != D3S_OK) return rc;
+  d3s_key sub;
+  take_subkey(nullptr, &sub);
+  r.key = sub;
+  rc = d3s_sample(ctx, &r, ctx->stream);
+  if (rc != D3S_OK) return rc;
+  int32_t *status = new int32_t[N];
+  e = cudaMemcpyAsync(out, ctx->ids_dev, (size_t)N * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                      ctx->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(status, ctx->status_dev, (size_t)N * sizeof(int32_t),
+                        cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    delete[] status;
+    return cuda_fail(e, "d3_sample");
+  }
+  int bad = 0;
+  for (int i = 0; i < N; i++) bad += status[i] != D3S_ROW_OK;
+  delete[] status;
+  if (bad) return fail(D3S_ERR_NONFINITE, "%d row(s) had non-finite logits", bad);
+  return D3S_OK;
+}
+
+void d3_sample(const float *logits, int N, int V, float temperature, int top_k, float top_p,
+               unsigned long long seed, int *out) {
+  const int rc = d3_sample_impl(logits, N, V, temperature, top_k, top_p, seed, out);
+  g_last_status = rc;
+  if (rc != D3S_OK && rc != D3S_ERR_NONFINITE && out)
+    for (int i = 0; i < N; i++) out[i] = -1;
+}
+
+int d3s_last_status(void) { return g_last_status; }
+
+}  // extern "C"

@@ -1,0 +1,296 @@
+"""ctypes binding of libd3s.so, the B200 sampler's C ABI (include/d3s.h).
+
+The host-side mirror of drama3-mlx's sampling interface:
+  - sample(logits, temperature, top_k, top_p, seed)   -> d3_sample (src/testapi.c:155-166),
+    the call the reference's tests make through tests/d3.py:211-217;
+  - Context.sample_top_k_top_p / sample_with_noise / sample_noise
+    -> src/sampling.c:179-209 on CUDA tensors;
+  - Context.sample_rows -> the batched engine (per-row parameters and seeds).
+
+There is no CPU fallback: without the library or a CUDA device every call
+raises. torch is used only to hold device memory and streams.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("D3S_LIB", PKG / "lib" / "libd3s.so"))
+
+D3S_OK = 0
+D3S_ERR_ARG = -1
+D3S_ERR_CUDA = -2
+D3S_ERR_NONFINITE = -3
+D3S_ERR_UNSUPPORTED = -4
+D3S_ERR_NOMEM = -5
+F32 = 0
+BF16 = 1
+ROW_OK, ROW_NONFINITE, ROW_BADPARAM = 0, 1, 2
+NOISE_KEY, NOISE_SEEDS, NOISE_GIVEN = 0, 1, 2
+MAX_V = 131072
+MAX_K = 16384
+
+# every symbol include/d3s.h declares
+EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split", "d3s_seed",
+           "d3s_next_key", "d3s_ctx_create", "d3s_ctx_destroy", "d3s_ctx_reserve",
+           "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
+           "d3s_debug_math", "d3_sample", "d3s_last_status")
+
+
+class D3SError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"d3s error {code}: {msg}")
+        self.code = code
+
+
+class Key(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_uint32 * 2)]
+
+    def tolist(self):
+        return [int(self.k[0]), int(self.k[1])]
+
+
+class Request(ctypes.Structure):
+    _fields_ = [
+        ("logits", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("N", ctypes.c_int32),
+        ("V", ctypes.c_int32), ("ld", ctypes.c_int64), ("temperature", ctypes.c_float),
+        ("top_p", ctypes.c_float), ("top_k", ctypes.c_int32),
+        ("temperature_rows", ctypes.c_void_p), ("top_p_rows", ctypes.c_void_p),
+        ("top_k_rows", ctypes.c_void_p), ("noise", ctypes.c_int32), ("key", Key),
+        ("seeds", ctypes.c_void_p), ("u", ctypes.c_void_p), ("ld_u", ctypes.c_int64),
+        ("ids", ctypes.c_void_p), ("status", ctypes.c_void_p), ("kept", ctypes.c_void_p),
+        ("probs", ctypes.c_void_p), ("topk_ids", ctypes.c_void_p), ("ld_out", ctypes.c_int64),
+    ]
+
+
+_lib = None
+
+
+def build() -> Path:
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("d3s_build", PKG / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build()
+
+
+def lib() -> ctypes.CDLL:
+    """Load libd3s.so (building it first if the sources are newer)."""
+    global _lib
+    if _lib is None:
+        if "D3S_LIB" not in os.environ:
+            build()
+        if not LIB_PATH.exists():
+            raise D3SError(D3S_ERR_UNSUPPORTED, f"{LIB_PATH} is missing; run drama3-mlx_b200/build.py")
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, i32, i64, f32, u64 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float,
+                                  ctypes.c_uint64)
+        kp = ctypes.POINTER(Key)
+        L.d3s_version.restype = i32
+        L.d3s_last_error.restype = ctypes.c_char_p
+        L.d3s_key_from_seed.argtypes = [u64, kp]
+        L.d3s_key_split.argtypes = [kp, kp, kp]
+        L.d3s_seed.argtypes = [kp, u64]
+        L.d3s_next_key.argtypes = [kp, kp]
+        L.d3s_ctx_create.argtypes = [i32, ctypes.POINTER(vp)]
+        L.d3s_ctx_destroy.argtypes = [vp]
+        L.d3s_ctx_destroy.restype = None
+        L.d3s_ctx_reserve.argtypes = [vp, i64]
+        L.d3s_sample_noise.argtypes = [vp, kp, i32, i32, i32, vp, vp]
+        L.d3s_sample_with_noise.argtypes = [vp, vp, i32, i32, i32, i64, vp, i32, i64, f32, f32, vp,
+                                            vp]
+        L.d3s_sample_top_k_top_p.argtypes = [vp, vp, i32, i32, i32, i64, f32, i32, f32, kp, vp, vp]
+        L.d3s_sample.argtypes = [vp, ctypes.POINTER(Request), vp]
+        L.d3s_debug_math.argtypes = [vp, i32, vp, vp, i64, vp]
+        L.d3_sample.argtypes = [ctypes.POINTER(ctypes.c_float), i32, i32, f32, i32, f32,
+                                ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_int32)]
+        L.d3_sample.restype = None
+        L.d3s_last_status.restype = i32
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != D3S_OK:
+        raise D3SError(rc, lib().d3s_last_error().decode())
+
+
+# ---- keys (host) ----
+
+def key_from_seed(seed: int) -> Key:
+    k = Key()
+    _check(lib().d3s_key_from_seed(seed, ctypes.byref(k)))
+    return k
+
+
+def key_split(key: Key) -> tuple[Key, Key]:
+    a, b = Key(), Key()
+    _check(lib().d3s_key_split(ctypes.byref(key), ctypes.byref(a), ctypes.byref(b)))
+    return a, b
+
+
+def seed(s: int, state: Key | None = None) -> None:
+    """m_seed: seeds `state`, or the library's global key when None."""
+    _check(lib().d3s_seed(ctypes.byref(state) if state is not None else None, s))
+
+
+def next_key(state: Key | None = None) -> Key:
+    sub = Key()
+    _check(lib().d3s_next_key(ctypes.byref(state) if state is not None else None, ctypes.byref(sub)))
+    return sub
+
+
+# ---- the reference's test entry point ----
+
+def sample(logits: np.ndarray, temperature, top_k, top_p, seed) -> np.ndarray:
+    """d3_sample on host arrays, as the reference's tests/d3.py sample() calls it."""
+    L = lib()
+    logits = np.ascontiguousarray(logits, np.float32)
+    out = np.zeros(len(logits), np.int32)
+    L.d3_sample(logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), logits.shape[0],
+                logits.shape[1], temperature, top_k, top_p, seed,
+                out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+    rc = L.d3s_last_status()
+    if rc not in (D3S_OK, D3S_ERR_NONFINITE):
+        _check(rc)
+    return out
+
+
+def last_status() -> int:
+    return lib().d3s_last_status()
+
+
+# ---- device API on torch tensors ----
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"logits must be float32 or bfloat16, got {t.dtype}")
+
+
+class Context:
+    """A d3s_ctx on one CUDA device (scratch + staging)."""
+
+    def __init__(self, device: int = 0):
+        import torch
+        if not torch.cuda.is_available():
+            raise D3SError(D3S_ERR_CUDA, "no CUDA device: the sampler has no CPU path")
+        self.device = device
+        self._h = ctypes.c_void_p()
+        _check(lib().d3s_ctx_create(device, ctypes.byref(self._h)))
+
+    def close(self) -> None:
+        if self._h:
+            lib().d3s_ctx_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reserve(self, max_rows: int) -> None:
+        _check(lib().d3s_ctx_reserve(self._h, max_rows))
+
+    def sample(self, req: Request, stream=None) -> None:
+        _check(lib().d3s_sample(self._h, ctypes.byref(req), _stream_ptr(stream)))
+
+    def request(self, logits, ids, *, temperature=1.0, top_p=1.0, top_k=1, temperature_rows=None,
+                top_p_rows=None, top_k_rows=None, noise=NOISE_KEY, key: Key | None = None,
+                seeds=None, u=None, status=None, kept=None, probs=None, topk_ids=None) -> Request:
+        N, V = logits.shape
+        r = Request()
+        r.logits = _ptr(logits)
+        r.dtype = _dtype_code(logits)
+        r.N, r.V, r.ld = N, V, logits.stride(0)
+        r.temperature, r.top_p, r.top_k = float(temperature), float(top_p), int(top_k)
+        r.temperature_rows = _ptr(temperature_rows)
+        r.top_p_rows = _ptr(top_p_rows)
+        r.top_k_rows = _ptr(top_k_rows)
+        r.noise = noise
+        if key is not None:
+            r.key = key
+        r.seeds = _ptr(seeds)
+        r.u = _ptr(u)
+        r.ld_u = u.stride(0) if u is not None else 0
+        r.ids = _ptr(ids)
+        r.status = _ptr(status)
+        r.kept = _ptr(kept)
+        r.probs = _ptr(probs)
+        r.topk_ids = _ptr(topk_ids)
+        out = probs if probs is not None else topk_ids
+        r.ld_out = out.stride(0) if out is not None else 0
+        return r
+
+    def sample_top_k_top_p(self, logits, temperature: float, top_k: int, top_p: float,
+                           state: Key | None = None, ids=None, stream=None):
+        import torch
+        N, V = logits.shape
+        if ids is None:
+            ids = torch.empty(N, dtype=torch.int32, device=logits.device)
+        _check(lib().d3s_sample_top_k_top_p(self._h, _ptr(logits), _dtype_code(logits), N, V,
+                                            logits.stride(0), temperature, top_k, top_p,
+                                            ctypes.byref(state) if state is not None else None,
+                                            _ptr(ids), _stream_ptr(stream)))
+        return ids
+
+    def sample_with_noise(self, logits, u, temperature: float, top_p: float, ids=None,
+                          stream=None):
+        import torch
+        N, V = logits.shape
+        if ids is None:
+            ids = torch.empty(N, dtype=torch.int32, device=logits.device)
+        _check(lib().d3s_sample_with_noise(self._h, _ptr(logits), _dtype_code(logits), N, V,
+                                           logits.stride(0), _ptr(u), u.shape[1], u.stride(0),
+                                           temperature, top_p, _ptr(ids), _stream_ptr(stream)))
+        return ids
+
+    def sample_noise(self, rows: int, V: int, top_k: int, state: Key | None = None, stream=None):
+        import torch
+        k = min(top_k, V)
+        u = torch.empty(rows, k, dtype=torch.float32, device=f"cuda:{self.device}")
+        _check(lib().d3s_sample_noise(self._h, ctypes.byref(state) if state is not None else None,
+                                      rows, V, top_k, _ptr(u), _stream_ptr(stream)))
+        return u
+
+    def sample_rows(self, logits, ids, *, temperature, top_p, top_k, seeds, status=None,
+                    kept=None, stream=None) -> None:
+        """Per-row parameters (tensors or scalars) and per-row seeds (int64 tensor)."""
+        import torch
+
+        def split(x):
+            return (x, 0) if isinstance(x, torch.Tensor) else (None, x)
+
+        T, T0 = split(temperature)
+        P, P0 = split(top_p)
+        K, K0 = split(top_k)
+        req = self.request(logits, ids, temperature=T0, top_p=P0, top_k=K0 or 1,
+                           temperature_rows=T, top_p_rows=P, top_k_rows=K, noise=NOISE_SEEDS,
+                           seeds=seeds, status=status, kept=kept)
+        self.sample(req, stream)
+
+    def debug_math(self, op: int, x, stream=None):
+        import torch
+        y = torch.empty_like(x)
+        _check(lib().d3s_debug_math(self._h, op, _ptr(x), _ptr(y), x.numel(), _stream_ptr(stream)))
+        return y

@@ -1,0 +1,166 @@
+/* d3s.h - C ABI of the B200 token sampler (temperature -> top-k -> top-p ->
+ * exponential-race draw) that replaces drama3-mlx's src/sampling.c.
+ *
+ * Paths in citations are relative to the drama3-mlx project root.
+ *
+ * Semantics (identical to the CPU oracle in oracle/, bit for bit):
+ *   k = min(top_k, V); T = max(temperature, 1e-5); q = logits / T;
+ *   lse = max(q) + log(sum exp(q - max q)) over the whole row;
+ *   top k by (q desc, id asc); cum_r = inclusive float sum of exp(q_r - lse);
+ *   rank r > 0 is dropped when cum_r > top_p; survivors are re-softmaxed;
+ *   the winner is the first rank with the largest p_r / -log(1 - u_r).
+ *   u [N, k] comes from MLX's threefry key sequence, as mlx_random_uniform
+ *   would draw it (src/sampling.c:179-209, src/mlxu.c:769-774).
+ *
+ * Ids are positions into the last axis (int32), as the reference returns them.
+ * Every entry point returns D3S_OK (0) or a negative D3S_ERR_* code and never
+ * exits the process (the reference calls die() -> exit(1), src/mlxu.c:28-36);
+ * d3s_last_error() holds the message for the calling thread.
+ * Device pointers are CUDA device memory of the context's device; `stream` is
+ * a cudaStream_t (NULL = the legacy default stream). Calls on device pointers
+ * are asynchronous on `stream`.
+ */
+#ifndef D3S_H
+#define D3S_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define D3S_VERSION 1
+
+#if defined(__GNUC__)
+#define D3S_API __attribute__((visibility("default")))
+#else
+#define D3S_API
+#endif
+
+/* status codes */
+#define D3S_OK 0
+#define D3S_ERR_ARG -1          /* bad argument (null pointer, size, dtype, top_k < 1, ...) */
+#define D3S_ERR_CUDA -2         /* a CUDA runtime call failed */
+#define D3S_ERR_NONFINITE -3    /* a row's scaled logits were NaN / +inf / all -inf (sync calls) */
+#define D3S_ERR_UNSUPPORTED -4  /* a size beyond the documented limits */
+#define D3S_ERR_NOMEM -5        /* device or host allocation failed */
+
+/* logits element types */
+#define D3S_F32 0
+#define D3S_BF16 1
+
+/* per-row status values (d3s_request.status) */
+#define D3S_ROW_OK 0
+#define D3S_ROW_NONFINITE 1
+#define D3S_ROW_BADPARAM 2
+
+/* noise sources (d3s_request.noise) */
+#define D3S_NOISE_KEY 0    /* one key for the batch: u = uniform(key, [N, k]) */
+#define D3S_NOISE_SEEDS 1  /* row r draws as d3_sample(row r, seeds[r]) would */
+#define D3S_NOISE_GIVEN 2  /* u given: sample_with_noise */
+
+/* limits */
+#define D3S_MAX_V 131072      /* the full-row sum's fixed point holds V <= 2^17 */
+#define D3S_MAX_K 16384       /* k = min(top_k, V) */
+
+/* The RNG state: one threefry-2x32 key, a plain serialisable pair of words.
+ * This is MLX's random key (mlx/random.cpp): key(seed) = {seed >> 32, seed}. */
+typedef struct {
+  uint32_t k[2];
+} d3s_key;
+
+typedef struct d3s_ctx d3s_ctx;
+
+D3S_API int d3s_version(void);
+D3S_API const char *d3s_last_error(void);
+
+/* ---- keys (host-side; no device work) ---- */
+
+/* random::key(seed). */
+D3S_API int d3s_key_from_seed(uint64_t seed, d3s_key *out);
+/* random::split(key) -> (k0, k1). */
+D3S_API int d3s_key_split(const d3s_key *key, d3s_key *k0, d3s_key *k1);
+/* m_seed (src/mlxu.c:769) -> mlx_random_seed: state = key(seed). state NULL
+ * seeds the library's global key, as MLX's global key sequence. */
+D3S_API int d3s_seed(d3s_key *state, uint64_t seed);
+/* The global key sequence's next(): (state, sub) = split(state); NULL = global. */
+D3S_API int d3s_next_key(d3s_key *state, d3s_key *sub);
+
+/* ---- context ---- */
+
+/* A context owns the device id, scratch for the rows that need the wide
+ * selection path, and staging buffers for the host-pointer entry points. */
+D3S_API int d3s_ctx_create(int device, d3s_ctx **out);
+D3S_API void d3s_ctx_destroy(d3s_ctx *ctx);
+/* Pre-size the scratch for requests of up to max_rows rows with per-row top_k
+ * (d3s_request.top_k_rows). d3s_sample grows it on demand with cudaMalloc,
+ * which a CUDA graph capture cannot contain: reserve before capturing. */
+D3S_API int d3s_ctx_reserve(d3s_ctx *ctx, int64_t max_rows);
+
+/* ---- the reference's internal API (src/model.h:169-176) ---- */
+
+/* sample_noise (src/sampling.c:179-192): u_dev [rows, k], k = min(top_k, V),
+ * drawn from state (NULL = global key), which advances by one split. */
+D3S_API int d3s_sample_noise(d3s_ctx *ctx, d3s_key *state, int rows, int V, int top_k, float *u_dev,
+                     void *stream);
+
+/* sample_with_noise (src/sampling.c:194-203): logits_dev [N, ld] (dtype),
+ * u_dev [N, ld_u] of which the first k columns are used; ids_dev [N]. */
+D3S_API int d3s_sample_with_noise(d3s_ctx *ctx, const void *logits_dev, int dtype, int N, int V,
+                          int64_t ld, const float *u_dev, int k, int64_t ld_u, float temperature,
+                          float top_p, int32_t *ids_dev, void *stream);
+
+/* sample_top_k_top_p (src/sampling.c:205-209): one split of state (NULL =
+ * global key), u = uniform(sub, [N, k]) generated inside the kernel. */
+D3S_API int d3s_sample_top_k_top_p(d3s_ctx *ctx, const void *logits_dev, int dtype, int N, int V,
+                           int64_t ld, float temperature, int top_k, float top_p,
+                           d3s_key *state, int32_t *ids_dev, void *stream);
+
+/* ---- batched engine (all of the above lower to this) ---- */
+
+typedef struct {
+  const void *logits;         /* [N, ld] device */
+  int32_t dtype;              /* D3S_F32 / D3S_BF16 */
+  int32_t N, V;
+  int64_t ld;                 /* elements between rows, >= V */
+  float temperature, top_p;   /* used when the matching *_rows pointer is NULL */
+  int32_t top_k;
+  const float *temperature_rows; /* [N] device, optional */
+  const float *top_p_rows;       /* [N] device, optional */
+  const int32_t *top_k_rows;     /* [N] device, optional (not with D3S_NOISE_KEY) */
+  int32_t noise;              /* D3S_NOISE_* */
+  d3s_key key;                /* D3S_NOISE_KEY: the subkey that draws u [N, k] */
+  const uint64_t *seeds;      /* D3S_NOISE_SEEDS: [N] device */
+  const float *u;             /* D3S_NOISE_GIVEN: [N, ld_u] device */
+  int64_t ld_u;
+  int32_t *ids;               /* [N] device, required; -1 for a flagged row */
+  int32_t *status;            /* [N] device, optional: D3S_ROW_* */
+  int32_t *kept;              /* [N] device, optional: survivors of the top-p cut */
+  float *probs;               /* [N, ld_out] device, optional: race probabilities by rank */
+  int32_t *topk_ids;          /* [N, ld_out] device, optional: ids by rank */
+  int64_t ld_out;
+} d3s_request;
+
+D3S_API int d3s_sample(d3s_ctx *ctx, const d3s_request *req, void *stream);
+
+/* Test hook: y_dev = f(x_dev) with the kernels' own arithmetic; op 0 = exp,
+ * 1 = log, 2 = the full-row-sum term (exp, or 0 when its 2^n scale is
+ * subnormal). No counterpart in the reference. */
+D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
+                   void *stream);
+
+/* ---- the reference's test C-ABI (src/testapi.c:155-166) ---- */
+
+/* Host logits [N, V] f32 -> host ids [N]: seeds the global key with `seed`,
+ * then sample_top_k_top_p. Synchronous. A failure writes -1 ids and sets
+ * d3s_last_error(); d3s_last_status() returns the code of the last d3_sample. */
+D3S_API void d3_sample(const float *logits, int N, int V, float temperature, int top_k, float top_p,
+               unsigned long long seed, int *out);
+D3S_API int d3s_last_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

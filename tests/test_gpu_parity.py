@@ -1,0 +1,320 @@
+"""CUDA sampler vs the CPU oracle, through the C ABI (libd3s.so). Ids, kept
+counts, ranked ids and probabilities must be bit-identical; the only tolerance
+in this file is the statistical one of the distribution test."""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not torch.cuda.is_available():
+        pytest.fail("the gpu tests need a CUDA device")
+    import d3s
+    c = d3s.Context(0)
+    yield c
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def synth():
+    import synth as s
+    return s
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def host_logits(x):
+    import synth
+    return synth.to_host_logits(x)
+
+
+# ---- arithmetic ----
+
+def float_range(lo_bits, hi_bits, stride):
+    return np.arange(lo_bits, hi_bits, stride, dtype=np.uint64).astype(np.uint32).view(np.float32)
+
+
+@pytest.mark.parametrize("op,name", [(0, "exp"), (1, "log"), (2, "term")])
+def test_math_bitwise(ctx, oracle, op, name):
+    if name == "exp":  # every 7th float in [-104, 89] plus the edges
+        xs = [float_range(0x80000000, 0xC2D00001, 7), float_range(0x00000000, 0x42B20001, 7)]
+    elif name == "log":  # every 7th positive float, subnormals included
+        xs = [float_range(0x00000001, 0x7F800001, 7)]
+    else:  # every 3rd float in [-110, 0], dense around the flush boundary
+        xs = [float_range(0x80000000, 0xC2DC0001, 3), np.linspace(-88.5, -86.5, 2_000_001).astype(np.float32)]
+    extra = np.array([0.0, -0.0, 1.0, -1.0, -np.inf, 88.0, -87.33654, -87.33655, 1e-30, 3e38],
+                     np.float32)
+    x = np.concatenate(xs + [extra])
+    if name == "term":
+        x = -np.abs(x)
+    ref = {"exp": oracle.exp, "log": oracle.log, "term": oracle.exp_term}[name]
+    for chunk in np.array_split(x, max(1, len(x) // (1 << 24))):
+        got = ctx.debug_math(op, dev(chunk)).cpu().numpy()
+        want = ref(chunk)
+        same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+        if not same.all():
+            bad = np.flatnonzero(~same)[:5]
+            pytest.fail(f"{name}: {len(np.flatnonzero(~same))} mismatches, e.g. "
+                        f"{[(float(chunk[i]), float(got[i]), float(want[i])) for i in bad]}")
+
+
+@pytest.mark.parametrize("rows,V,top_k", [(1, 4097, 30), (3, 4097, 5), (7, 1024, 31), (256, 4097, 30),
+                                          (1000, 100, 64), (5, 3, 30)])
+def test_sample_noise_equals_oracle_uniform(ctx, oracle, rows, V, top_k):
+    import d3s
+    state = d3s.key_from_seed(rows * 1000 + top_k)
+    ostate = oracle.key_from_seed(rows * 1000 + top_k)
+    for _ in range(3):
+        u = ctx.sample_noise(rows, V, top_k, state).cpu().numpy()
+        want = oracle.uniform(oracle.next_key(ostate), rows * min(top_k, V)).reshape(rows, -1)
+        assert np.array_equal(u, want)
+    assert state.tolist() == ostate.tolist()
+
+
+# ---- the reference's test entry point ----
+
+def test_d3_sample_equals_oracle_and_golden(oracle):
+    import d3s
+    from pathlib import Path
+    g = np.load(Path(__file__).resolve().parent / "golden" / "oracle_cases.npz")
+    for pi, (T, k, p) in enumerate(g["d3_params"]):
+        for s in range(4):
+            ids = d3s.sample(g["d3_logits"], float(T), int(k), float(p), s)
+            assert ids.tolist() == g["d3_ids"][pi, s].tolist()
+        for s in range(4, 24):
+            assert (d3s.sample(g["d3_logits"], float(T), int(k), float(p), s).tolist()
+                    == oracle.d3_sample(g["d3_logits"], float(T), int(k), float(p), s).tolist())
+
+
+@pytest.mark.parametrize("V,top_k", [(4097, 30), (1024, 30), (4097, 5)])
+def test_ties_match_oracle(oracle, V, top_k):
+    """The reference's tests/test_decode.py:73-86 inputs: logits tied across the
+    k-th place, seeds 0..39, top-p off; equal to the oracle and to itself."""
+    import d3s
+    rng = np.random.default_rng(1)
+    logits = np.round(rng.standard_normal((8, V)) * 2).astype(np.float32)
+    for seed in range(40):
+        a = d3s.sample(logits, 1.0, top_k, 2.0, seed)
+        b = d3s.sample(logits, 1.0, top_k, 2.0, seed)
+        assert a.tolist() == b.tolist() == oracle.d3_sample(logits, 1.0, top_k, 2.0, seed).tolist()
+
+
+@pytest.mark.parametrize("T,top_k,top_p", [(0.7, 30, 0.7), (1.0, 30, 0.9), (1.0, 5, 1.0),
+                                           (0.3, 30, 0.95)])
+def test_distribution(oracle, T, top_k, top_p):
+    """tests/test_decode.py:89-114 restated on the GPU: 4000 seeds, frequencies
+    within 4 sigma + 1e-3 of the exact kept-set probabilities."""
+    import d3s
+    from test_oracle import kept_set_definition
+    rng = np.random.default_rng(0)
+    logits = (rng.standard_normal((1, 4097)) * 3).astype(np.float32)
+    n = 4000
+    ours = np.array([d3s.sample(logits, T, top_k, top_p, s)[0] for s in range(n)])
+    ids, probs, _ = kept_set_definition(logits[0], T, top_k, top_p)
+    expected = dict(zip(ids.tolist(), probs.tolist()))
+    for token, prob in expected.items():
+        tol = 4 * np.sqrt(prob * (1 - prob) / n) + 1e-3
+        assert abs(np.mean(ours == token) - prob) < tol
+    assert set(np.unique(ours).tolist()) <= set(expected)
+
+
+# ---- device API ----
+
+def run_given(ctx, x, u, T, p):
+    """sample_with_noise with every diagnostic output."""
+    import d3s
+    N, k = u.shape
+    ids = torch.empty(N, dtype=torch.int32, device="cuda")
+    status = torch.empty_like(ids)
+    kept = torch.empty_like(ids)
+    probs = torch.zeros(N, k, dtype=torch.float32, device="cuda")
+    topk = torch.zeros(N, k, dtype=torch.int32, device="cuda")
+    req = ctx.request(x, ids, temperature=T, top_p=p, top_k=k, noise=d3s.NOISE_GIVEN, u=u,
+                      status=status, kept=kept, probs=probs, topk_ids=topk)
+    ctx.sample(req)
+    torch.cuda.synchronize()
+    return ids.cpu().numpy(), status.cpu().numpy(), kept.cpu().numpy(), probs.cpu().numpy(), topk.cpu().numpy()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("V,k,T,p", [(4097, 30, 0.7, 0.7), (1024, 30, 1.0, 0.9), (4097, 64, 1.2, 0.5),
+                                     (4097, 1, 0.7, 0.7), (100, 100, 1.0, 2.0), (31, 7, 0.5, 0.9),
+                                     (1, 1, 1.0, 0.5), (4097, 300, 1.0, 0.95), (5000, 256, 0.8, 0.99)])
+def test_given_noise_diagnostics_bitwise(ctx, oracle, dtype, V, k, T, p):
+    rng = np.random.default_rng(V * 7 + k)
+    N = 48
+    x = (rng.standard_normal((N, V)) * 3).astype(np.float32)
+    xt = dev(x, torch.bfloat16 if dtype == "bf16" else torch.float32)
+    xh = host_logits(xt)
+    u = rng.random((N, k), dtype=np.float32)
+    u[0, 0] = 0.0
+    ids, status, kept, probs, topk = run_given(ctx, xt, dev(u), T, p)
+    xf = xh.astype(np.uint32).__lshift__(16).view(np.float32) if dtype == "bf16" else xh
+    for r in range(N):
+        rid, tids, oprobs, d = oracle.sample_row(xf[r], T, p, k, u[r])
+        assert ids[r] == rid and status[r] == 0 and kept[r] == d.kept, r
+        assert topk[r].tolist() == tids.tolist(), r
+        assert probs[r].view(np.uint32).tolist() == oprobs.view(np.uint32).tolist(), r
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("V,top_k", [(4097, 30), (1024, 30), (4097, 64), (4097, 4097), (20000, 30),
+                                     (8192, 256), (8193, 40), (2, 5)])
+def test_key_mode_matches_oracle(ctx, oracle, dtype, V, top_k):
+    """sample_top_k_top_p: one split of the state, u = uniform(sub, [N, k])."""
+    import d3s
+    rng = np.random.default_rng(V + top_k)
+    N = 40
+    x = (rng.standard_normal((N, V)) * 2.5).astype(np.float32)
+    xt = dev(x, torch.bfloat16 if dtype == "bf16" else torch.float32)
+    xh = host_logits(xt)
+    state = d3s.key_from_seed(V)
+    ostate = oracle.key_from_seed(V)
+    for _ in range(2):
+        ids = ctx.sample_top_k_top_p(xt, 0.8, top_k, 0.9, state)
+        want = oracle.sample_top_k_top_p(ostate, xh, 0.8, top_k, 0.9)
+        assert ids.cpu().numpy().tolist() == want.tolist()
+
+
+def test_rows_config2_bf16(ctx, oracle, synth):
+    x = synth.c2_logits(256, seed=3)
+    seeds = torch.arange(5000, 5256, device="cuda", dtype=torch.int64)
+    ids = torch.empty(256, dtype=torch.int32, device="cuda")
+    ctx.sample_rows(x, ids, temperature=0.7, top_p=0.7, top_k=30, seeds=seeds)
+    want = oracle.sample_rows(host_logits(x), 0.7, 0.7, 30, seeds.cpu().numpy().astype(np.uint64))
+    assert ids.cpu().numpy().tolist() == want.tolist()
+
+
+def test_rows_config4_heads(ctx, oracle, synth):
+    x = synth.c4_logits(512 * 9, seed=4)
+    seeds = torch.arange(512 * 9, device="cuda", dtype=torch.int64) * 7 + 1
+    ids = torch.empty(512 * 9, dtype=torch.int32, device="cuda")
+    ctx.sample_rows(x, ids, temperature=1.0, top_p=0.9, top_k=30, seeds=seeds)
+    want = oracle.sample_rows(host_logits(x), 1.0, 0.9, 30, seeds.cpu().numpy().astype(np.uint64))
+    assert ids.cpu().numpy().tolist() == want.tolist()
+
+
+def test_rows_config5_per_row_params(ctx, oracle, synth):
+    x, T, p, k, seeds = synth.c5_batch(4096, seed=5)
+    ids = torch.empty(4096, dtype=torch.int32, device="cuda")
+    kept = torch.empty_like(ids)
+    ctx.sample_rows(x, ids, temperature=T, top_p=p, top_k=k, seeds=seeds, kept=kept)
+    want = oracle.sample_rows(host_logits(x), T.cpu().numpy(), p.cpu().numpy(), k.cpu().numpy(),
+                              seeds.cpu().numpy().astype(np.uint64))
+    assert ids.cpu().numpy().tolist() == want.tolist()
+
+
+def test_per_row_k_above_fast_limit_is_deferred(ctx, oracle):
+    """Rows with k > 256 go through the wide kernel's hand-off list; a second
+    launch checks the list counters were re-zeroed."""
+    rng = np.random.default_rng(8)
+    N, V = 300, 4097
+    x = (rng.standard_normal((N, V)) * 2).astype(np.float32)
+    k = rng.integers(1, 65, N).astype(np.int32)
+    k[::7] = rng.integers(257, 5000, len(k[::7]))
+    seeds = np.arange(N, dtype=np.int64) + 17
+    for rep in range(2):
+        ids = torch.empty(N, dtype=torch.int32, device="cuda")
+        ctx.sample_rows(dev(x), ids, temperature=0.9, top_p=0.97, top_k=dev(k), seeds=dev(seeds))
+        want = oracle.sample_rows(x, 0.9, 0.97, k, seeds.astype(np.uint64))
+        assert ids.cpu().numpy().tolist() == want.tolist(), rep
+
+
+def test_exact_selection_path_for_massive_ties(ctx, oracle):
+    """All-equal and few-valued rows put more than the candidate buffer at the
+    threshold: the kernel falls back to the exact 64-bit key bisection."""
+    import d3s
+    N, V = 16, 4097
+    x = np.zeros((N, V), np.float32)
+    x[1] = np.tile([1.0, 0.0], V)[:V]
+    x[2, 100:3000] = 5.0
+    x[3] = np.arange(V) % 3
+    x[4, :] = -0.0
+    x[5, ::2] = 0.0
+    x[5, 1::2] = -0.0
+    u = np.random.default_rng(2).random((N, 64), dtype=np.float32)
+    ids, status, kept, probs, topk = run_given(ctx, dev(x), dev(u), 1.0, 0.8)
+    for r in range(N):
+        rid, tids, oprobs, d = oracle.sample_row(x[r], 1.0, 0.8, 64, u[r])
+        assert ids[r] == rid and topk[r].tolist() == tids.tolist(), r
+        assert probs[r].view(np.uint32).tolist() == oprobs.view(np.uint32).tolist()
+
+
+def test_nonfinite_rows_are_flagged(ctx, oracle):
+    import d3s
+    rng = np.random.default_rng(3)
+    N, V = 8, 4097
+    x = (rng.standard_normal((N, V)) * 3).astype(np.float32)
+    x[1, 5] = np.nan
+    x[2, 7] = np.inf
+    x[3] = -np.inf
+    x[4, ::2] = -np.inf  # masked tokens are fine
+    x[5, 9] = -np.nan
+    u = rng.random((N, 30), dtype=np.float32)
+    ids, status, kept, probs, topk = run_given(ctx, dev(x), dev(u), 0.7, 0.9)
+    assert status.tolist() == [0, 1, 1, 1, 0, 1, 0, 0]
+    assert ids[[1, 2, 3, 5]].tolist() == [-1] * 4
+    for r in (0, 4, 6, 7):
+        assert ids[r] == oracle.sample_row(x[r], 0.7, 0.9, 30, u[r])[0]
+    out = np.zeros(N, np.int32)
+    ids_sync = d3s.sample(x, 0.7, 30, 0.9, 1)
+    assert d3s.last_status() == d3s.D3S_ERR_NONFINITE and ids_sync[1] == -1
+
+
+def test_bad_params(ctx):
+    import d3s
+    x = torch.zeros(4, 64, device="cuda")
+    with pytest.raises(d3s.D3SError):
+        ctx.sample_top_k_top_p(x, 1.0, 0, 0.9)
+    with pytest.raises(d3s.D3SError):
+        ctx.sample_top_k_top_p(x, float("nan"), 5, 0.9)
+    k = torch.tensor([5, 0, 3, -1], dtype=torch.int32, device="cuda")
+    T = torch.tensor([1.0, 1.0, float("nan"), 1.0], device="cuda")
+    ids = torch.empty(4, dtype=torch.int32, device="cuda")
+    status = torch.empty_like(ids)
+    req = ctx.request(x, ids, temperature_rows=T, top_p=0.9, top_k_rows=k, noise=d3s.NOISE_SEEDS,
+                      seeds=torch.arange(4, device="cuda"), status=status)
+    ctx.sample(req)
+    assert status.cpu().tolist() == [0, 2, 2, 2] and ids.cpu().tolist()[1:] == [-1, -1, -1]
+
+
+def test_strided_rows_and_empty_batch(ctx, oracle):
+    rng = np.random.default_rng(4)
+    big = (rng.standard_normal((10, 5000)) * 2).astype(np.float32)
+    xt = dev(big)[:, 100:4197]  # ld = 5000 > V = 4097
+    u = rng.random((10, 30), dtype=np.float32)
+    ids = run_given(ctx, xt, dev(u), 0.7, 0.8)[0]
+    for r in range(10):
+        assert ids[r] == oracle.sample_row(big[r, 100:4197], 0.7, 0.8, 30, u[r])[0]
+    empty = torch.zeros(0, 4097, device="cuda")
+    assert ctx.sample_top_k_top_p(empty, 1.0, 30, 0.9).numel() == 0
+
+
+def test_full_size_config5(ctx, oracle, synth):
+    """65536 x 4097 f32 with per-row parameters: deterministic, in range, every
+    id among its row's top-k by value, and a random subset equal to the oracle."""
+    x, T, p, k, seeds = synth.c5_batch(65536, seed=11)
+    ids = torch.empty(65536, dtype=torch.int32, device="cuda")
+    ids2 = torch.empty_like(ids)
+    ctx.sample_rows(x, ids, temperature=T, top_p=p, top_k=k, seeds=seeds)
+    ctx.sample_rows(x, ids2, temperature=T, top_p=p, top_k=k, seeds=seeds)
+    assert torch.equal(ids, ids2)
+    assert int(ids.min()) >= 0 and int(ids.max()) < 4097
+    picked = x.gather(1, ids.long()[:, None])[:, 0]
+    kth = torch.topk(x, 64, dim=1).values.gather(1, (k.long() - 1)[:, None])[:, 0]
+    assert bool((picked >= kth).all())
+    rows = np.random.default_rng(0).choice(65536, 400, replace=False)
+    rows_t = torch.from_numpy(rows).cuda()
+    want = oracle.sample_rows(host_logits(x[rows_t]), T[rows_t].cpu().numpy(), p[rows_t].cpu().numpy(),
+                              k[rows_t].cpu().numpy(), seeds[rows_t].cpu().numpy().astype(np.uint64))
+    assert ids[rows_t].cpu().numpy().tolist() == want.tolist()

@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-latency", action="store_true")
     return ap.parse_args()
 
 
@@ -336,7 +337,8 @@ def run_ours(args):
     cpu = None
     latency = None
     if rank == 0 and world == 1:
-        latency = c1_latency(ctx, torch)
+        if not args.no_latency:
+            latency = c1_latency(ctx, torch)
         if not args.no_cpu_baseline:
             n = min(rows, 16384)
             cpu = cpu_baseline(synth.to_host_logits(x[:n]), T[:n].cpu().numpy(), p[:n].cpu().numpy(),

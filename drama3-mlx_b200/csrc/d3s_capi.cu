@@ -151,6 +151,7 @@ d3s::KArgs to_kargs(const d3s_request *r, const d3s_ctx *ctx) {
   a.deferred = ctx->scratch.deferred;
   a.deferred_n = ctx->scratch.counters;
   a.wide_done = ctx->scratch.counters ? ctx->scratch.counters + 1 : nullptr;
+  a.deferred_cap = ctx->scratch.capacity;
   return a;
 }
 

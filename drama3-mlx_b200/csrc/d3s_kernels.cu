@@ -196,7 +196,13 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const KArgs a) {
       continue;
     }
     if (rp.k > kFastMaxK) {  // handed to the wide kernel
-      if (t == 0) a.deferred[atomicAdd(a.deferred_n, 1u)] = row;
+      if (t == 0) {
+        const unsigned pos = atomicAdd(a.deferred_n, 1u);
+        if (pos < (unsigned long long)a.deferred_cap)
+          a.deferred[pos] = row;
+        else
+          flag_row(a, row, D3S_ROW_BADPARAM);
+      }
       continue;
     }
     const void *base = row_base<BF16>(a, row);
@@ -321,7 +327,9 @@ __global__ void __launch_bounds__(kThreads) sample_wide_kernel(const KArgs a, in
   float *scr = reinterpret_cast<float *>(keys + kp_cap);
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int V = a.V;
-  const unsigned nrows = use_list ? *((volatile uint32_t *)a.deferred_n) : (unsigned)a.N;
+  const unsigned nrows =
+      use_list ? (unsigned)min((long long)*((volatile uint32_t *)a.deferred_n), (long long)a.deferred_cap)
+               : (unsigned)a.N;
   for (unsigned idx = blockIdx.x; idx < nrows; idx += gridDim.x) {
     const int row = use_list ? a.deferred[idx] : (int)idx;
     RowP rp;

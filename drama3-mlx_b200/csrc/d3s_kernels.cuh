@@ -35,6 +35,7 @@ struct KArgs {
   int32_t *deferred;
   uint32_t *deferred_n;
   uint32_t *wide_done;
+  int64_t deferred_cap;  // entries of `deferred`; hand-offs beyond it flag the row
 };
 
 // Device scratch a launch needs: `deferred` holds N int32, counters 2 uint32

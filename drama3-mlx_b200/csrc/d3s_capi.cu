@@ -67,8 +67,8 @@ int reserve_scratch(d3s_ctx *ctx, int64_t rows) {
   cudaError_t e = cudaMalloc(&d, (size_t)cap * sizeof(int32_t));
   if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e));
   if (!ctx->scratch.counters) {
-    e = cudaMalloc(&c, 2 * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(c, 0, 2 * sizeof(uint32_t));
+    e = cudaMalloc(&c, 3 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c, 0, 3 * sizeof(uint32_t));
     if (e != cudaSuccess) {
       cudaFree(d);
       if (c) cudaFree(c);
@@ -152,6 +152,7 @@ d3s::KArgs to_kargs(const d3s_request *r, const d3s_ctx *ctx) {
   a.deferred_n = ctx->scratch.counters;
   a.wide_done = ctx->scratch.counters ? ctx->scratch.counters + 1 : nullptr;
   a.deferred_cap = ctx->scratch.capacity;
+  a.error = ctx->scratch.counters ? reinterpret_cast<int32_t *>(ctx->scratch.counters + 2) : nullptr;
   return a;
 }
 
@@ -331,11 +332,40 @@ int d3s_sample_top_k_top_p(d3s_ctx *ctx, const void *logits_dev, int dtype, int 
 }
 
 int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
-                   void *stream) {
-  if (!ctx || op < 0 || op > 2 || n < 0) return fail(D3S_ERR_ARG, "bad math args");
+                   float param, void *stream) {
+  if (!ctx || op < 0 || op > 3 || n < 0) return fail(D3S_ERR_ARG, "bad math args");
   DeviceGuard g(ctx->device);
-  const int rc = d3s::launch_math(op, x_dev, y_dev, n, (cudaStream_t)stream);
+  const int rc = d3s::launch_math(op, x_dev, y_dev, n, param, (cudaStream_t)stream);
   if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "math launch");
+  return D3S_OK;
+}
+
+int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64_t lo, uint64_t hi,
+                        uint64_t step, unsigned long long *bad_dev, float *example_dev,
+                        void *stream) {
+  if (!ctx || !T_dev || nT < 0 || step == 0 || hi < lo || hi > (1ull << 32) || !bad_dev ||
+      !example_dev)
+    return fail(D3S_ERR_ARG, "bad division-check args");
+  DeviceGuard g(ctx->device);
+  const int rc = d3s::launch_div_check(T_dev, nT, lo, hi, step, bad_dev, example_dev,
+                                       (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "division check launch");
+  return D3S_OK;
+}
+
+int d3s_ctx_check(d3s_ctx *ctx) {
+  if (!ctx) return fail(D3S_ERR_ARG, "null ctx");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "device");
+  if (!ctx->scratch.counters) return D3S_OK;
+  uint32_t err = 0;
+  e = cudaMemcpy(&err, ctx->scratch.counters + 2, sizeof(err), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "error word");
+  if (err) {
+    cudaMemset(ctx->scratch.counters + 2, 0, sizeof(uint32_t));
+    return fail(D3S_ERR_CUDA, "a sampler kernel gave up waiting for a row copy (rows left unsampled)");
+  }
   return D3S_OK;
 }
 
@@ -428,6 +458,8 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
   int bad = 0;
   for (int i = 0; i < N; i++) bad += status[i] != D3S_ROW_OK;
   delete[] status;
+  rc = d3s_ctx_check(ctx);
+  if (rc != D3S_OK) return rc;
   if (bad) return fail(D3S_ERR_NONFINITE, "%d row(s) had non-finite logits", bad);
   return D3S_OK;
 }

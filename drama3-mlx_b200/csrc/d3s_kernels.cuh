@@ -36,10 +36,13 @@ struct KArgs {
   uint32_t *deferred_n;
   uint32_t *wide_done;
   int64_t deferred_cap;  // entries of `deferred`; hand-offs beyond it flag the row
+  int32_t *error;        // set to 1 when a bounded wait gives up
 };
 
-// Device scratch a launch needs: `deferred` holds N int32, counters 2 uint32
-// that must be zero before the first launch (the wide kernel re-zeroes them).
+// Device scratch a launch needs: `deferred` holds N int32; counters holds 3
+// uint32 that must be zero before the first launch: the hand-off count and the
+// wide kernel's completion count (the wide kernel re-zeroes both), and the
+// error word (cleared by the host when it reads it).
 struct Scratch {
   int32_t *deferred = nullptr;
   uint32_t *counters = nullptr;
@@ -52,7 +55,14 @@ int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t stream);
 // Draw u [rows, k] = uniform(key, rows * k) (sample_noise).
 int launch_uniform(uint2 key, int rows, int k, float *u, cudaStream_t stream);
 
-// Debug: y = exp_full(x) (op 0), log_full(x) (op 1), exp_term(x) (op 2) on device.
-int launch_math(int op, const float *x, float *y, int64_t n, cudaStream_t stream);
+// Debug: y = exp_full(x) (op 0), log_full(x) (op 1), exp_term(x) (op 2), or the
+// per-row-reciprocal quotient x / T (op 3) on device.
+int launch_math(int op, const float *x, float *y, int64_t n, float T, cudaStream_t stream);
+
+// Debug: count x in [lo, hi) (float bit patterns, step `step`, within the
+// reciprocal path's range) whose reciprocal-path quotient x / T differs from the
+// IEEE quotient, for each T of Ts[nT]; adds to *bad, last failure in example[2].
+int launch_div_check(const float *Ts, int nT, uint64_t lo, uint64_t hi, uint64_t step,
+                     unsigned long long *bad, float *example, cudaStream_t stream);
 
 }  // namespace d3s

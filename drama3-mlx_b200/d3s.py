@@ -39,7 +39,8 @@ MAX_K = 16384
 EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split", "d3s_seed",
            "d3s_next_key", "d3s_ctx_create", "d3s_ctx_destroy", "d3s_ctx_reserve",
            "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
-           "d3s_debug_math", "d3_sample", "d3s_last_status")
+           "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3_sample",
+           "d3s_last_status")
 
 
 class D3SError(RuntimeError):
@@ -106,7 +107,9 @@ def lib() -> ctypes.CDLL:
                                             vp]
         L.d3s_sample_top_k_top_p.argtypes = [vp, vp, i32, i32, i32, i64, f32, i32, f32, kp, vp, vp]
         L.d3s_sample.argtypes = [vp, ctypes.POINTER(Request), vp]
-        L.d3s_debug_math.argtypes = [vp, i32, vp, vp, i64, vp]
+        L.d3s_debug_math.argtypes = [vp, i32, vp, vp, i64, f32, vp]
+        L.d3s_debug_div_check.argtypes = [vp, vp, i32, u64, u64, u64, vp, vp, vp]
+        L.d3s_ctx_check.argtypes = [vp]
         L.d3_sample.argtypes = [ctypes.POINTER(ctypes.c_float), i32, i32, f32, i32, f32,
                                 ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_int32)]
         L.d3_sample.restype = None
@@ -289,8 +292,23 @@ class Context:
                            seeds=seeds, status=status, kept=kept)
         self.sample(req, stream)
 
-    def debug_math(self, op: int, x, stream=None):
+    def check(self) -> None:
+        """Synchronise and raise if a kernel recorded a failure (a bounded wait)."""
+        _check(lib().d3s_ctx_check(self._h))
+
+    def debug_math(self, op: int, x, param: float = 1.0, stream=None):
         import torch
         y = torch.empty_like(x)
-        _check(lib().d3s_debug_math(self._h, op, _ptr(x), _ptr(y), x.numel(), _stream_ptr(stream)))
+        _check(lib().d3s_debug_math(self._h, op, _ptr(x), _ptr(y), x.numel(), param,
+                                    _stream_ptr(stream)))
         return y
+
+    def debug_div_check(self, Ts, lo: int = 0, hi: int = 1 << 32, step: int = 1, stream=None):
+        """(mismatch count, example (x, T)) of the reciprocal-path division."""
+        import torch
+        bad = torch.zeros(1, dtype=torch.int64, device=Ts.device)
+        ex = torch.zeros(2, dtype=torch.float32, device=Ts.device)
+        _check(lib().d3s_debug_div_check(self._h, _ptr(Ts), Ts.numel(), lo, hi, step, _ptr(bad),
+                                         _ptr(ex), _stream_ptr(stream)))
+        torch.cuda.synchronize()
+        return int(bad.item()), ex.cpu().tolist()

@@ -144,11 +144,22 @@ typedef struct {
 
 D3S_API int d3s_sample(d3s_ctx *ctx, const d3s_request *req, void *stream);
 
-/* Test hook: y_dev = f(x_dev) with the kernels' own arithmetic; op 0 = exp,
- * 1 = log, 2 = the full-row-sum term (exp, or 0 when its 2^n scale is
- * subnormal). No counterpart in the reference. */
+/* Synchronise the context's device and report a failure the kernels recorded
+ * (a bounded wait that gave up); clears it. D3S_OK when none. */
+D3S_API int d3s_ctx_check(d3s_ctx *ctx);
+
+/* Test hooks (no counterpart in the reference): y_dev = f(x_dev) with the
+ * kernels' own arithmetic; op 0 = exp, 1 = log, 2 = the full-row-sum term (exp,
+ * or 0 when its 2^n scale is subnormal), 3 = x / param by the per-row
+ * reciprocal path. */
 D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
-                   void *stream);
+                           float param, void *stream);
+/* Counts float bit patterns x in [lo, hi) (step `step`) inside the reciprocal
+ * path's range whose quotient x / T differs from the IEEE quotient, for each of
+ * T_dev[nT]; adds to *bad_dev (device), last failing (x, T) in example_dev[2]. */
+D3S_API int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64_t lo,
+                                uint64_t hi, uint64_t step, unsigned long long *bad_dev,
+                                float *example_dev, void *stream);
 
 /* ---- the reference's test C-ABI (src/testapi.c:155-166) ---- */
 

@@ -68,6 +68,25 @@ def test_math_bitwise(ctx, oracle, op, name):
                         f"{[(float(chunk[i]), float(got[i]), float(want[i])) for i in bad]}")
 
 
+def test_reciprocal_division_is_ieee(ctx):
+    """The fast kernel divides by a per-row reciprocal with one correction step
+    when the row's |x| range allows it; that quotient must equal the IEEE one
+    for every float x in the range: all 2^32 bit patterns for 64 temperatures,
+    every 61st pattern for 1024 more."""
+    rng = np.random.default_rng(12)
+    special = np.array([1e-5, 0.5, 0.7, 1.0, 1.2, 2.0 ** -20, 2.0 ** 20, 3.0, 1 / 3, 0.1, 10.0,
+                        np.float32(1) - np.float32(2 ** -24), 2 - 2 ** -23, 1 + 2 ** -23, 1.5, 0.3],
+                       np.float32)
+    special = np.concatenate([special, np.array([0x3f7fffff, 0x3fffffff, 0x3effffff, 0x4f7fffff,
+                                                 0x3f000001], np.uint32).view(np.float32)])
+    full = np.concatenate([special, rng.uniform(0.5, 1.2, 64 - len(special)).astype(np.float32)])
+    bad, ex = ctx.debug_div_check(torch.from_numpy(full).cuda())
+    assert bad == 0, ex
+    more = np.concatenate([rng.uniform(0.5, 1.2, 512), np.exp(rng.uniform(np.log(2.0 ** -20), np.log(2.0 ** 20), 512))])
+    bad, ex = ctx.debug_div_check(torch.from_numpy(more.astype(np.float32)).cuda(), step=61)
+    assert bad == 0, ex
+
+
 @pytest.mark.parametrize("rows,V,top_k", [(1, 4097, 30), (3, 4097, 5), (7, 1024, 31), (256, 4097, 30),
                                           (1000, 100, 64), (5, 3, 30)])
 def test_sample_noise_equals_oracle_uniform(ctx, oracle, rows, V, top_k):
@@ -169,7 +188,8 @@ def test_given_noise_diagnostics_bitwise(ctx, oracle, dtype, V, k, T, p):
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("V,top_k", [(4097, 30), (1024, 30), (4097, 64), (4097, 4097), (20000, 30),
-                                     (8192, 256), (8193, 40), (2, 5)])
+                                     (8192, 256), (8193, 40), (2, 5), (256, 30), (257, 64),
+                                     (511, 128), (3072, 129), (4096, 200), (6000, 17), (300, 300)])
 def test_key_mode_matches_oracle(ctx, oracle, dtype, V, top_k):
     """sample_top_k_top_p: one split of the state, u = uniform(sub, [N, k])."""
     import d3s
@@ -288,16 +308,27 @@ def test_bad_params(ctx):
     assert status.cpu().tolist() == [0, 2, 2, 2] and ids.cpu().tolist()[1:] == [-1, -1, -1]
 
 
-def test_strided_rows_and_empty_batch(ctx, oracle):
-    rng = np.random.default_rng(4)
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("off", [100, 3, 1])
+def test_strided_and_unaligned_rows(ctx, oracle, dtype, off):
+    """ld > V and row starts off any 16-byte boundary (the bulk copy fetches
+    the aligned span around each row)."""
+    rng = np.random.default_rng(4 + off)
     big = (rng.standard_normal((10, 5000)) * 2).astype(np.float32)
-    xt = dev(big)[:, 100:4197]  # ld = 5000 > V = 4097
+    bt = dev(big, torch.bfloat16 if dtype == "bf16" else torch.float32)
+    xt = bt[:, off:off + 4097]  # ld = 5000 > V = 4097
+    xh = host_logits(xt)
+    xf = (xh.astype(np.uint32) << 16).view(np.float32) if dtype == "bf16" else xh
     u = rng.random((10, 30), dtype=np.float32)
     ids = run_given(ctx, xt, dev(u), 0.7, 0.8)[0]
     for r in range(10):
-        assert ids[r] == oracle.sample_row(big[r, 100:4197], 0.7, 0.8, 30, u[r])[0]
+        assert ids[r] == oracle.sample_row(xf[r], 0.7, 0.8, 30, u[r])[0]
+
+
+def test_empty_batch_and_ctx_check(ctx):
     empty = torch.zeros(0, 4097, device="cuda")
     assert ctx.sample_top_k_top_p(empty, 1.0, 30, 0.9).numel() == 0
+    ctx.check()
 
 
 def test_full_size_config5(ctx, oracle, synth):
@@ -318,3 +349,4 @@ def test_full_size_config5(ctx, oracle, synth):
     want = oracle.sample_rows(host_logits(x[rows_t]), T[rows_t].cpu().numpy(), p[rows_t].cpu().numpy(),
                               k[rows_t].cpu().numpy(), seeds[rows_t].cpu().numpy().astype(np.uint64))
     assert ids[rows_t].cpu().numpy().tolist() == want.tolist()
+    ctx.check()

@@ -59,7 +59,31 @@ struct DeviceGuard {
   }
 };
 
+int reserve_records(d3s_ctx *ctx, int64_t rows) {
+  if (ctx->scratch.rec_capacity >= rows) return D3S_OK;
+  const int64_t cap = std::max<int64_t>(rows, 1024);
+  d3s::RowHead *h = nullptr;
+  d3s::RowCands *c = nullptr;
+  cudaError_t e = cudaMalloc(&h, (size_t)cap * sizeof(d3s::RowHead));
+  if (e == cudaSuccess) e = cudaMalloc(&c, (size_t)cap * sizeof(d3s::RowCands));
+  if (e != cudaSuccess) {
+    if (h) cudaFree(h);
+    return fail(D3S_ERR_NOMEM, "row records: %s", cudaGetErrorString(e));
+  }
+  if (ctx->scratch.heads) {
+    cudaDeviceSynchronize();  // the old records may be in use by queued work
+    cudaFree(ctx->scratch.heads);
+    cudaFree(ctx->scratch.cands);
+  }
+  ctx->scratch.heads = h;
+  ctx->scratch.cands = c;
+  ctx->scratch.rec_capacity = cap;
+  return D3S_OK;
+}
+
 int reserve_scratch(d3s_ctx *ctx, int64_t rows) {
+  const int rc = reserve_records(ctx, rows);
+  if (rc != D3S_OK) return rc;
   if (ctx->scratch.capacity >= rows) return D3S_OK;
   int64_t cap = std::max<int64_t>(rows, 1024);
   int32_t *d = nullptr;
@@ -249,6 +273,8 @@ void d3s_ctx_destroy(d3s_ctx *ctx) {
   cudaDeviceSynchronize();
   cudaFree(ctx->scratch.deferred);
   cudaFree(ctx->scratch.counters);
+  cudaFree(ctx->scratch.heads);
+  cudaFree(ctx->scratch.cands);
   cudaFree(ctx->h_logits_dev);
   cudaFree(ctx->ids_dev);
   cudaFree(ctx->status_dev);
@@ -262,10 +288,8 @@ int d3s_sample(d3s_ctx *ctx, const d3s_request *req, void *stream) {
   if (rc != D3S_OK) return rc;
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
-  if (req->top_k_rows) {
-    rc = reserve_scratch(ctx, req->N);
-    if (rc != D3S_OK) return rc;
-  }
+  rc = reserve_scratch(ctx, req->N);
+  if (rc != D3S_OK) return rc;
   const d3s::KArgs a = to_kargs(req, ctx);
   rc = d3s::launch_sample(a, ctx->scratch, (cudaStream_t)stream);
   if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "sampler launch");

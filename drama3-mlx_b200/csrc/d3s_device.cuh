@@ -78,10 +78,22 @@ __device__ __forceinline__ float exp_full(float x) {
   return __fmul_rn(__fmul_rn(p, s1), s2);
 }
 
-// One term of the full-row sum, d = q - max in [-inf, 0] (never NaN): equals
-// exp_full(d) when its 2^n scale is normal (n >= -126), else 0.
+// One term of the full-row sum for d = q - max in [-inf, 0] (never NaN):
+// exp(max(d, -87)). Below -87 the term (< 2^-125) is far under the 2^-46
+// resolution of the fixed-point sum; the clamp keeps the 2^n scale normal
+// (n >= -126), so the scale is (n + 127) << 23 = (t's bits << 23) + (127 << 23)
+// (t = 1.5 * 2^23 + n, whose bits are 0x4B400000 + n; 0x4B400000 << 23 wraps
+// to 0) and the result p * 2^n rounds once, as exp_full's does.
+// (n + 127) << 23 from t's bits, as one integer multiply-add.
+__device__ __forceinline__ float term_scale(float t) {
+  unsigned r;
+  asm("mad.lo.u32 %0, %1, 8388608, 1065353216;" : "=r"(r) : "r"(__float_as_uint(t)));
+  return __uint_as_float(r);
+}
+
+constexpr float kTermFloor = -87.0f;
 __device__ __forceinline__ float exp_term(float d) {
-  d = fmaxf(d, -110.0f);
+  d = fmaxf(d, kTermFloor);
   float t = __fmaf_rn(d, kL2E, kShifter);
   float nf = __fsub_rn(t, kShifter);
   float r = __fmaf_rn(-nf, kLn2Hi, d);
@@ -94,16 +106,17 @@ __device__ __forceinline__ float exp_term(float d) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  int a = (int)(__float_as_uint(t) - (kShifterBits - 127u));  // n + 127
-  a = max(a, 0);
-  return __fmul_rn(p, __uint_as_float((unsigned)a << 23));
+  return __fmul_rn(p, term_scale(t));
 }
 
 // Two terms at once on the packed fp32x2 pipe (sm_100a); same roundings as
-// exp_term, element by element.
+// exp_term, element by element. CLAMP = false when the caller knows d >= -87.
+template <bool CLAMP>
 __device__ __forceinline__ float2 exp_term2(float2 d) {
-  d.x = fmaxf(d.x, -110.0f);
-  d.y = fmaxf(d.y, -110.0f);
+  if (CLAMP) {
+    d.x = fmaxf(d.x, kTermFloor);
+    d.y = fmaxf(d.y, kTermFloor);
+  }
   const float2 l2e = make_float2(kL2E, kL2E), sh = make_float2(kShifter, kShifter);
   float2 t = __ffma2_rn(d, l2e, sh);
   float2 nf = __fadd2_rn(t, make_float2(-kShifter, -kShifter));
@@ -118,10 +131,7 @@ __device__ __forceinline__ float2 exp_term2(float2 d) {
   p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
   p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
   p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
-  int ax = max((int)(__float_as_uint(t.x) - (kShifterBits - 127u)), 0);
-  int ay = max((int)(__float_as_uint(t.y) - (kShifterBits - 127u)), 0);
-  float2 s = make_float2(__uint_as_float((unsigned)ax << 23), __uint_as_float((unsigned)ay << 23));
-  return __fmul2_rn(p, s);
+  return __fmul2_rn(p, make_float2(term_scale(t.x), term_scale(t.y)));
 }
 
 // log: x = 2^e m, m in (sqrt2/2, sqrt2], s = (m-1)/(m+1), log m = 2 atanh(s)
@@ -201,6 +211,18 @@ __host__ __device__ __forceinline__ uint32_t bits_word(uint2 key, uint64_t n, ui
   if (o && f == h) return threefry2x32(key, make_uint2((uint32_t)h, 0u)).x;
   const uint64_t g = f - h - o;
   return threefry2x32(key, make_uint2((uint32_t)g, (uint32_t)(h + o + g))).y;
+}
+
+// bits_word with one threefry evaluation: the counter pair and the output
+// half are selected first, so the hash is inlined once.
+__device__ __forceinline__ uint32_t bits_word1(uint2 key, uint64_t n, uint64_t f) {
+  const uint64_t h = n >> 1, o = n & 1;
+  const bool odd_mid = o && f == h;
+  const bool first = f < h || odd_mid;
+  const uint64_t g = first ? f : f - h - o;
+  const uint32_t c1 = odd_mid ? 0u : (uint32_t)(h + o + g);
+  const uint2 r = threefry2x32(key, make_uint2((uint32_t)g, c1));
+  return first ? r.x : r.y;
 }
 
 // random::key(seed)

@@ -32,7 +32,6 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kPartials = 256;
 constexpr int kCandCap = 256;    // fast kernel candidate buffer
-constexpr int kSortMax = 256;    // warp bitonic sort up to 8 keys per lane
 constexpr int kFastMaxK = 256;
 constexpr int kFastW = 4;        // warps per CTA in the fast kernel
 constexpr int kFastThreads = 32 * kFastW;
@@ -62,14 +61,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
                "r"(bytes)
                : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
-                                         uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
@@ -161,7 +152,7 @@ __device__ __forceinline__ float row_uniform(const KArgs &a, int row, int k, int
   const bool one = a.noise == D3S_NOISE_KEY;
   const uint64_t n = one ? (uint64_t)a.N * (uint64_t)k : (uint64_t)k;
   const uint64_t f = one ? (uint64_t)row * (uint64_t)k + (uint64_t)r : (uint64_t)r;
-  return bits_to_uniform(bits_word(key, n, f));
+  return bits_to_uniform(bits_word1(key, n, f));
 }
 
 // q = x / T, correctly rounded, from rT = RN(1/T): q0 = RN(x rT) is within an
@@ -178,18 +169,19 @@ __device__ __forceinline__ float div_rows(float x, float rT, float mT) {
   const float e = __fmaf_rn(q0, mT, x);
   return __fmaf_rn(e, rT, q0);
 }
-// Range in which div_rows is exact: nonzero |x| in [2^-60, 2^60], T in [2^-20, 2^20].
-__device__ __forceinline__ bool div_rows_ok(float amin, float amax, float T) {
-  return amin >= 0x1p-60f && amax <= 0x1p60f && T >= 0x1p-20f && T <= 0x1p20f;
+// Rows on which div_rows gives every quotient that can matter exactly. The
+// reciprocal step is exact for |x| in [2^-100, 2^60] with T in [2^-17, 2^20]
+// (checked over every float x for a set of T by the tests). Smaller nonzero
+// |x| may be off by an ulp, but with |max| >= 2^-40 their term is exp(-max)
+// (|q| < 2^-83 is below half an ulp of max) and with |tau| >= 2^-60 they are
+// never a boundary candidate; candidate keys themselves use the IEEE divide.
+__device__ __forceinline__ bool div_rows_ok(float xmin, float xmax, float T, float gmax,
+                                            float tau) {
+  return fmaxf(fabsf(xmin), fabsf(xmax)) <= 0x1p60f && T >= 0x1p-17f && T <= 0x1p20f &&
+         fabsf(gmax) >= 0x1p-40f && fabsf(tau) >= 0x1p-60f;
 }
 
 // ---- warp helpers ----
-
-__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
-  const unsigned lo = __shfl_xor_sync(kFull, (unsigned)v, m);
-  const unsigned hi = __shfl_xor_sync(kFull, (unsigned)(v >> 32), m);
-  return ((unsigned long long)hi << 32) | lo;
-}
 
 // Sum of the 2^-46 fixed-point partial sums of one warp (each lane's value
 // < 2^52): the low 26 and high bits are reduced separately so the 32-bit
@@ -220,107 +212,55 @@ __device__ __forceinline__ float warp_rth_largest(float (&v)[M], int r) {
   }
 }
 
-// Bitonic sort of 32 * S keys held as v[s] = element lane + 32 s, descending.
-template <int S>
-__device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int lane) {
-  constexpr int n = 32 * S;
-#pragma unroll
-  for (int size = 2; size <= n; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride >= 32) {
-        const int ss = stride / 32;
-#pragma unroll
-        for (int s = 0; s < S; ++s) {
-          if ((s & ss) == 0) {
-            const bool desc = ((lane + 32 * s) & size) == 0;
-            const unsigned long long x = v[s], y = v[s | ss];
-            const bool swap = desc ? (x < y) : (x > y);
-            v[s] = swap ? y : x;
-            v[s | ss] = swap ? x : y;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int s = 0; s < S; ++s) {
-          const unsigned long long o = shfl_xor_u64(v[s], stride);
-          const bool desc = ((lane + 32 * s) & size) == 0;
-          const bool lower = (lane & stride) == 0;
-          const bool keep_max = lower == desc;
-          const unsigned long long mx = v[s] > o ? v[s] : o, mn = v[s] > o ? o : v[s];
-          v[s] = keep_max ? mx : mn;
-        }
-      }
-    }
-  }
-}
-
-// Sort keys[0..C) (C <= 32 S) descending in place with one warp; pads with 0.
-template <int S>
-__device__ __forceinline__ void warp_sort_smem(unsigned long long *keys, int C, int lane) {
-  unsigned long long v[S];
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const int e = lane + 32 * s;
-    v[s] = e < C ? keys[e] : 0ull;
-  }
-  __syncwarp();
-  warp_sort_desc<S>(v, lane);
-#pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const int e = lane + 32 * s;
-    if (e < C) keys[e] = v[s];
-  }
-  __syncwarp();
-}
-
-__device__ __forceinline__ void warp_sort_any(unsigned long long *keys, int C, int lane) {
-  if (C <= 32)
-    warp_sort_smem<1>(keys, C, lane);
-  else if (C <= 64)
-    warp_sort_smem<2>(keys, C, lane);
-  else if (C <= 128)
-    warp_sort_smem<4>(keys, C, lane);
-  else
-    warp_sort_smem<8>(keys, C, lane);
-}
-
 // The serial end of a row, run by one warp: sorted[k] holds the top-k keys in
-// rank order, scr[k] is scratch. Inclusive cumsum of exp(v - lse) in rank
-// order (src/sampling.c:39, :126-127), drop when cum > top_p at rank > 0
-// (:40-43, :128), softmax over the survivors with a 1/sum multiply (:44,
-// :129-134), race p / -log(1 - u) where the first strictly greater score wins
-// (:45-47, :135-137). Survivors form a prefix of the ranks and every survivor's
-// score is positive unless its noise is -0, so the dropped ranks (p = 0, score
-// 0 or NaN) are only drawn when no survivor scored above 0.
-__device__ void sample_tail(const KArgs &a, int row, const unsigned long long *sorted, float *scr,
-                            int k, float lse, float top_p, int lane) {
+// rank order, scr (>= k + 4 floats, 16-byte aligned) is scratch, key draws the
+// row's uniforms. Inclusive cumsum of exp(v - lse) in rank order
+// (src/sampling.c:39, :126-127), drop when cum > top_p at rank > 0 (:40-43,
+// :128), softmax over the survivors with a 1/sum multiply (:44, :129-134), race
+// p / -log(1 - u) where the first strictly greater score wins (:45-47,
+// :135-137). The two sequential sums run identically on every lane (broadcast
+// reads, four ranks per load). Survivors are a prefix of the ranks and every
+// survivor's score is positive unless its noise is -0, so the dropped ranks
+// (p = 0, score 0 or NaN) are drawn only when no survivor scored above 0.
+__device__ __forceinline__ void sample_tail(const KArgs &a, int row, uint2 key,
+                                         const unsigned long long *sorted, float *scr, int k,
+                                         float lse, float top_p, int lane) {
   for (int r = lane; r < k; r += 32) scr[r] = exp_full(__fsub_rn(cand_value(sorted[r]), lse));
   __syncwarp();
   int kept = k;
-  if (lane == 0) {
+  {
     float cum = 0.0f;
-    for (int r = 0; r < k; ++r) {
-      cum = __fadd_rn(cum, scr[r]);
-      if (r > 0 && cum > top_p) {
-        kept = r;
-        break;
+    for (int r0 = 0; r0 < k; r0 += 4) {
+      const float4 e4 = *reinterpret_cast<const float4 *>(scr + r0);
+      const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+      bool stop = false;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = r0 + i;
+        if (!stop && r < k) {
+          cum = __fadd_rn(cum, ev[i]);
+          if (r > 0 && cum > top_p) {
+            kept = r;
+            stop = true;
+          }
+        }
       }
+      if (stop) break;
     }
   }
-  kept = __shfl_sync(kFull, kept, 0);
   __syncwarp();
   const float top = cand_value(sorted[0]);
   for (int r = lane; r < kept; r += 32) scr[r] = exp_full(__fsub_rn(cand_value(sorted[r]), top));
   __syncwarp();
-  float inv = 0.0f;
-  if (lane == 0) {
-    float sum = 0.0f;
-    for (int r = 0; r < kept; ++r) sum = __fadd_rn(sum, scr[r]);
-    inv = __fdiv_rn(1.0f, sum);
+  float sum = 0.0f;
+  for (int r0 = 0; r0 < kept; r0 += 4) {
+    const float4 e4 = *reinterpret_cast<const float4 *>(scr + r0);
+    const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (r0 + i < kept) sum = __fadd_rn(sum, ev[i]);
   }
-  inv = __shfl_sync(kFull, inv, 0);
-  const uint2 key = a.noise == D3S_NOISE_GIVEN ? make_uint2(0u, 0u) : row_key(a, row);
+  const float inv = __fdiv_rn(1.0f, sum);
   float best = -1.0f;
   int best_r = 0;
   for (int r = lane; r < kept; r += 32) {
@@ -357,234 +297,312 @@ __device__ void sample_tail(const KArgs &a, int row, const unsigned long long *s
   }
 }
 
-// ---- fast kernel ----
-
-struct alignas(16) FastSmem {
-  uint64_t mbar[kMaxStages];
-  float red_max[kFastW];
-  float red_amax[kFastW];
-  float red_amin[kFastW];
-  float red_tau[kFastW];
-  unsigned long long red_sum[kFastW];
-  int red_cnt[2][kFastW];
-  unsigned cand_n[2];  // by row parity: row it+1's counter is cleared during row it
-  unsigned long long cand[kCandCap];
-  float scr[kCandCap];
+// Per-row parameters as stored (read one row ahead of use).
+struct RawP {
+  float T, p;
+  int tk;
+  unsigned long long seed;
 };
 
-// Issue the bulk copy of row `row` into stage s: the 16-byte-aligned span that
+__device__ __forceinline__ RawP load_raw(const KArgs &a, int row) {
+  RawP r;
+  r.T = a.T_rows ? a.T_rows[row] : a.T;
+  r.p = a.p_rows ? a.p_rows[row] : a.top_p;
+  r.tk = a.k_rows ? a.k_rows[row] : a.top_k;
+  r.seed = a.noise == D3S_NOISE_SEEDS ? a.seeds[row] : 0ull;
+  return r;
+}
+
+__device__ __forceinline__ int resolve(const KArgs &a, const RawP &r, RowP &rp) {
+  if (r.tk < 1 || r.T != r.T) return D3S_ROW_BADPARAM;
+  const int k = min(r.tk, a.V);
+  if (k > D3S_MAX_K) return D3S_ROW_BADPARAM;
+  rp.T = r.T < kMinTemperature ? kMinTemperature : r.T;
+  rp.p = r.p;
+  rp.k = k;
+  return D3S_ROW_OK;
+}
+
+// ---- stats kernel (K1): the streaming pass over the rows ----
+
+constexpr int kStatMinBlocks = 5;
+
+struct alignas(16) StatSmem {
+  uint64_t mbar[kMaxStages];
+  unsigned stage_done[kMaxStages];  // warps finished with the stage's row
+  unsigned cand_n[kMaxStages];      // candidates of the stage's row so far
+  float red_max[2][kFastW];         // by row parity, so no barrier is needed between rows
+  float red_min[2][kFastW];
+  float red_tau[2][kFastW];
+};
+
+// L2 policy for the logits stream: read once, so evict it first and keep the
+// row records the select kernel reads next.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Issue the bulk copy of row `row` into a stage: the 16-byte-aligned span that
 // covers the row (a copy must start and end on 16-byte boundaries).
 template <int ESZ>
 __device__ __forceinline__ void issue_row(const KArgs &a, int row, unsigned char *stage,
-                                          uint64_t *bar) {
+                                          uint64_t *bar, uint64_t pol) {
   const uintptr_t start = (uintptr_t)a.logits + (uintptr_t)row * (uintptr_t)a.ld * ESZ;
   const uintptr_t lo = start & ~(uintptr_t)15;
   const uintptr_t hi = (start + (uintptr_t)a.V * ESZ + 15) & ~(uintptr_t)15;
   const uint32_t bytes = (uint32_t)(hi - lo);
   mbar_expect_tx(bar, bytes);
-  bulk_g2s(stage, reinterpret_cast<const void *>(lo), bytes, bar);
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(stage)),
+      "l"(lo), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+      : "memory");
 }
 
-template <int JJ, bool BF16>
-__global__ void __launch_bounds__(kFastThreads) sample_fast_kernel(const KArgs a, int stages,
-                                                                    int span) {
+__device__ __forceinline__ void defer_row(const KArgs &a, int row) {
+  const unsigned pos = atomicAdd(a.deferred_n, 1u);
+  if (pos < (unsigned long long)a.deferred_cap)
+    a.deferred[pos] = row;
+  else
+    flag_row(a, row, D3S_ROW_BADPARAM);
+}
+
+// The rest of a row once its max and threshold are known: q = x / T in place
+// (per-row reciprocal when the range allows, IEEE divide otherwise), the two
+// packed partial sums of exp(q - max) in fixed point, and every element >= tau
+// written as a (value, id) key into this warp's slots: a bit per element in
+// registers, one warp prefix sum, then a short loop over the set bits that
+// re-reads x from the stage and recomputes its q.
+template <int JJ, bool CLAMP, bool EXACT>
+__device__ __forceinline__ void sum_and_mask(const float (&q)[kFastPP][JJ], float gmax, float tau,
+                                             int t, int V, float2 &s2,
+                                             unsigned long long &bits) {
+  constexpr int PP = kFastPP;
+  constexpr int NT = kFastThreads;
+  const float2 mg = make_float2(-gmax, -gmax);
+#pragma unroll
+  for (int j = 0; j < JJ; ++j) {
+    float2 e = exp_term2<CLAMP>(__fadd2_rn(make_float2(q[0][j], q[PP - 1][j]), mg));
+    if (!(EXACT && j < JJ - 1)) {  // a column that can run past V: padding adds exactly 0
+      if (t + kPartials * j >= V) e.x = 0.0f;
+      if (t + NT * (PP - 1) + kPartials * j >= V) e.y = 0.0f;
+    }
+    s2 = __fadd2_rn(s2, e);
+#pragma unroll
+    for (int m = 0; m < PP; ++m)
+      if (q[m][j] >= tau && ((EXACT && j < JJ - 1) || t + NT * m + kPartials * j < V))
+        bits |= 1ull << (m * JJ + j);
+  }
+}
+
+template <int JJ, bool BF16, bool EXACT>
+__device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &Cs,
+                                          unsigned *cand_n, const unsigned char *rb,
+                                          float (&q)[kFastPP][JJ], float T, float gmax, float tau,
+                                          float xmin, bool fast, int t, int lane, int w) {
+  constexpr int PP = kFastPP;
+  constexpr int NT = kFastThreads;
+  const int V = a.V;
+  if (fast) {
+    const float rT = __frcp_rn(T);
+    const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-T, -T);
+#pragma unroll
+    for (int j = 0; j < JJ; ++j) {
+      const float2 r2 = div_rows2(make_float2(q[0][j], q[PP - 1][j]), rT2, mT2);
+      q[0][j] = r2.x;
+      q[PP - 1][j] = r2.y;
+    }
+#pragma unroll
+    for (int m = 0; m < PP; ++m)  // padding past V stays -inf (only the last column has any)
+      if (t + NT * m + kPartials * (JJ - 1) >= V) q[m][JJ - 1] = -f_inf();
+  } else {
+#pragma unroll
+    for (int m = 0; m < PP; ++m)
+#pragma unroll
+      for (int j = 0; j < JJ; ++j) q[m][j] = __fdiv_rn(q[m][j], T);
+  }
+  float2 s2 = make_float2(0.0f, 0.0f);
+  unsigned long long bits = 0ull;
+  // every term's d >= the row's smallest d: when that is >= -87 the floor is a no-op
+  if (__fsub_rn(__fdiv_rn(xmin, T), gmax) >= kTermFloor)
+    sum_and_mask<JJ, false, EXACT>(q, gmax, tau, t, V, s2, bits);
+  else
+    sum_and_mask<JJ, true, EXACT>(q, gmax, tau, t, V, s2, bits);
+  const unsigned long long wsum = warp_sum_fixed(__float2ull_rz(__fmul_rn(s2.x, 0x1p46f)) +
+                                                 __float2ull_rz(__fmul_rn(s2.y, 0x1p46f)));
+  const int mine = __popcll(bits);
+  int incl = mine;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(kFull, incl, d);
+    if (lane >= d) incl += o;
+  }
+  // this warp's span of the row's list: one shared-memory atomic per warp
+  unsigned base = 0;
+  if (lane == 31 && incl > 0) base = atomicAdd(cand_n, (unsigned)incl);
+  base = __shfl_sync(kFull, base, 31);
+  int pos = (int)base + incl - mine;
+  while (bits) {
+    const int b = __ffsll((long long)bits) - 1;
+    bits &= bits - 1;
+    const int m = b / JJ, j = b - m * JJ;
+    const int i = t + NT * m + kPartials * j;
+    const float qi = __fdiv_rn(lds_x<BF16>(rb, i), T);
+    if (pos < kCandCap) Cs.cand[pos] = cand_key(qi, (uint32_t)i);
+    ++pos;
+  }
+  if (lane == 31) H.sum[w] = wsum;
+  if (t == 0) {
+    H.gmax = gmax;
+    H.done = 0;
+  }
+}
+
+// The r-th largest of the warp's 32 lane maxima (r <= 32), by a bitonic sort.
+__device__ __forceinline__ float warp_rth_of32(float v, int r, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const float o = __shfl_xor_sync(kFull, v, stride);
+      const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
+      v = keep_max ? fmaxf(v, o) : fminf(v, o);
+    }
+  return __shfl_sync(kFull, v, r - 1);
+}
+
+// Per row: x from the stage into registers, max / |x| range / per-warp
+// candidate threshold, one barrier; then stats_row; the last warp to finish
+// with a stage refills it with the row `stages` ahead.
+// EXACT: JJ == ceil(V / 256), so only the last column can run past V.
+template <int JJ, bool BF16, bool EXACT>
+__global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
+    sample_stats_kernel(const KArgs a, RowHead *heads, RowCands *cands, int stages, int span) {
   extern __shared__ __align__(128) unsigned char dsm[];
-  __shared__ FastSmem sm;
+  __shared__ StatSmem sm;
   constexpr int PP = kFastPP;
   constexpr int NT = kFastThreads;
   constexpr int ESZ = BF16 ? 2 : 4;
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int V = a.V;
+  const uint64_t pol = evict_first_policy();
   if (t == 0) {
-    for (int s = 0; s < stages; ++s) mbar_init(&sm.mbar[s], 1);
-    sm.cand_n[0] = 0;
-    sm.cand_n[1] = 0;
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&sm.mbar[s], 1);
+      sm.stage_done[s] = 0;
+      sm.cand_n[s] = 0;
+    }
     fence_mbar_init();
   }
   __syncthreads();
   if (t == 0)
     for (int s = 0; s < stages; ++s) {
       const int r = blockIdx.x + s * gridDim.x;
-      if (r < a.N) issue_row<ESZ>(a, r, dsm + (size_t)s * span, &sm.mbar[s]);
+      if (r < a.N) issue_row<ESZ>(a, r, dsm + (size_t)s * span, &sm.mbar[s], pol);
     }
+  RawP nxt;
+  if ((int)blockIdx.x < a.N) nxt = load_raw(a, blockIdx.x);
   int it = 0;
   bool failed = false;
   for (;; ++it) {
     const int row = blockIdx.x + it * gridDim.x;
     if (row >= a.N) break;
-    const int s = it % stages;
+    const RawP cur = nxt;
+    if (row + (int)gridDim.x < a.N) nxt = load_raw(a, row + gridDim.x);
+    RowP rp;
+    const int pst = resolve(a, cur, rp);
+    const int s = it % stages, par = it & 1;
     const bool ok = mbar_wait_bounded(&sm.mbar[s], (uint32_t)(it / stages) & 1u);
     const unsigned char *rb =
         dsm + (size_t)s * span +
         (((uintptr_t)a.logits + (uintptr_t)row * (uintptr_t)a.ld * ESZ) & 15);
-    // ---- the row into registers; its max and |x| range ----
     float q[PP][JJ];
     float pm[PP];
-    float amax = 0.0f, amin = f_inf();
+    float pmn = f_inf();
 #pragma unroll
     for (int m = 0; m < PP; ++m) {
       pm[m] = -f_inf();
 #pragma unroll
       for (int j = 0; j < JJ; ++j) {
         const int i = t + NT * m + kPartials * j;
-        const bool valid = ok && i < V;
+        const bool valid = (EXACT && j < JJ - 1) || i < V;
         const float v = valid ? lds_x<BF16>(rb, i) : -f_inf();
         q[m][j] = v;
         pm[m] = max_nan(pm[m], v);
-        if (valid) {
-          amax = fmaxf(amax, fabsf(v));
-          amin = fminf(amin, fabsf(v));
-        }
+        if (valid) pmn = fminf(pmn, v);
       }
     }
     {
-      const float wm = warp_max_nan(max_nan(pm[0], pm[PP - 1]));
-      const float wa = warp_max(amax);
-      const float wi = -warp_max(-amin);
+      const float lm = max_nan(pm[0], pm[PP - 1]);
+      const float wm = warp_max_nan(lm);
+      const float wi = -warp_max(-pmn);
+      // candidate threshold in x: the ceil(k/4)-th largest lane maximum of this
+      // warp (each of those lanes holds an element at least that large); x / T
+      // is monotone, so the threshold in q is RN(min over warps / T)
+      float tw = -f_inf();
+      if (pst == D3S_ROW_OK && rp.k <= kFastMaxK && wm == wm) {
+        const int r = (rp.k + kFastW - 1) / kFastW;
+        if (r <= 32) {
+          tw = warp_rth_of32(lm, r, lane);
+        } else {
+          float v2[PP];
+#pragma unroll
+          for (int m = 0; m < PP; ++m) v2[m] = pm[m];
+          tw = warp_rth_largest<PP>(v2, r);
+        }
+      }
       if (lane == 0) {
-        sm.red_max[w] = wm;
-        sm.red_amax[w] = wa;
-        sm.red_amin[w] = wi;
+        sm.red_max[par][w] = wm;
+        sm.red_min[par][w] = wi;
+        sm.red_tau[par][w] = tw;
       }
     }
     if (__syncthreads_or(!ok)) {
       failed = true;
       break;
     }
-    if (t == 0 && row + stages * (int)gridDim.x < a.N) {  // the stage is free: refill it
-      fence_proxy_async();
-      issue_row<ESZ>(a, row + stages * gridDim.x, dsm + (size_t)s * span, &sm.mbar[s]);
-    }
-    RowP rp;
-    const int pst = row_params(a, row, rp);
-    if (pst != D3S_ROW_OK) {
-      if (t == 0) flag_row(a, row, pst);
-      continue;
-    }
-    if (rp.k > kFastMaxK) {  // handed to the wide kernel
-      if (t == 0) {
-        const unsigned pos = atomicAdd(a.deferred_n, 1u);
-        if (pos < (unsigned long long)a.deferred_cap)
-          a.deferred[pos] = row;
-        else
-          flag_row(a, row, D3S_ROW_BADPARAM);
+    RowHead &H = heads[row];
+    if (pst == D3S_ROW_OK && rp.k <= kFastMaxK) {
+      float xmax = sm.red_max[par][0], xmin = sm.red_min[par][0], taux = sm.red_tau[par][0];
+#pragma unroll
+      for (int i = 1; i < kFastW; ++i) {
+        xmax = max_nan(xmax, sm.red_max[par][i]);
+        xmin = fminf(xmin, sm.red_min[par][i]);
+        taux = fminf(taux, sm.red_tau[par][i]);
       }
-      continue;
-    }
-    float xmax = sm.red_max[0], xamax = sm.red_amax[0], xamin = sm.red_amin[0];
-#pragma unroll
-    for (int i = 1; i < kFastW; ++i) {
-      xmax = max_nan(xmax, sm.red_max[i]);
-      xamax = fmaxf(xamax, sm.red_amax[i]);
-      xamin = fminf(xamin, sm.red_amin[i]);
-    }
-    const float gmax = __fdiv_rn(xmax, rp.T);  // max(x / T) = RN(max(x) / T): RN is monotone
-    if (!(fabsf(gmax) < f_inf())) {             // NaN, +inf, or every value -inf
-      if (t == 0) flag_row(a, row, D3S_ROW_NONFINITE);
-      __syncthreads();
-      continue;
-    }
-    // ---- q = x / T ----
-    if (div_rows_ok(xamin, xamax, rp.T)) {
-      const float rT = __frcp_rn(rp.T);
-      const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-rp.T, -rp.T);
-#pragma unroll
-      for (int j = 0; j < JJ; ++j) {
-        const float2 r2 = div_rows2(make_float2(q[0][j], q[PP - 1][j]), rT2, mT2);
-        q[0][j] = r2.x;
-        q[PP - 1][j] = r2.y;
+      const float gmax = __fdiv_rn(xmax, rp.T);  // max(x / T) = RN(max(x) / T): RN is monotone
+      const float tau = __fdiv_rn(taux, rp.T);
+      if (fabsf(gmax) < f_inf())
+        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q, rp.T, gmax, tau,
+                                   xmin, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);
+      else if (t == 0) {  // NaN, +inf, or every value -inf
+        flag_row(a, row, D3S_ROW_NONFINITE);
+        H.done = 1;
       }
-#pragma unroll
-      for (int m = 0; m < PP; ++m)  // padding past V stays -inf (only the last column has any)
-        if (t + NT * m + kPartials * (JJ - 1) >= V) q[m][JJ - 1] = -f_inf();
-    } else {
-#pragma unroll
-      for (int m = 0; m < PP; ++m)
-#pragma unroll
-        for (int j = 0; j < JJ; ++j) q[m][j] = __fdiv_rn(q[m][j], rp.T);
+    } else if (t == 0) {
+      if (pst != D3S_ROW_OK)
+        flag_row(a, row, pst);
+      else
+        defer_row(a, row);
+      H.done = 1;
     }
-    float pq[PP];
-#pragma unroll
-    for (int m = 0; m < PP; ++m) pq[m] = __fdiv_rn(pm[m], rp.T);
-    // ---- partials t and t + 128 of the full-row sum, one packed chain ----
-    float2 s2 = make_float2(0.0f, 0.0f);
-    const float2 mg = make_float2(-gmax, -gmax);
-#pragma unroll
-    for (int j = 0; j < JJ; ++j)
-      s2 = __fadd2_rn(s2, exp_term2(__fadd2_rn(make_float2(q[0][j], q[PP - 1][j]), mg)));
-    const unsigned long long fx =
-        __float2ull_rz(__fmul_rn(s2.x, 0x1p46f)) + __float2ull_rz(__fmul_rn(s2.y, 0x1p46f));
-    const unsigned long long wsum = warp_sum_fixed(fx);
-    // candidate threshold: each warp's ceil(k/4)-th largest partial max, min over warps
-    const float tau_w = warp_rth_largest<PP>(pq, (rp.k + kFastW - 1) / kFastW);
+    // this warp is done with the stage; the last of the four refills it
+    __syncwarp();
     if (lane == 0) {
-      sm.red_sum[w] = wsum;
-      sm.red_tau[w] = tau_w;
-    }
-    if (t == 0) sm.cand_n[(it + 1) & 1] = 0;
-    __syncthreads();
-    unsigned long long S = 0;
-    float tau = f_inf();
-#pragma unroll
-    for (int i = 0; i < kFastW; ++i) {
-      S += sm.red_sum[i];
-      tau = fminf(tau, sm.red_tau[i]);
-    }
-    const float lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
-    // ---- candidates: every element >= tau (at least k of them) ----
-    unsigned *cn = &sm.cand_n[it & 1];
-#pragma unroll
-    for (int m = 0; m < PP; ++m)
-#pragma unroll
-      for (int j = 0; j < JJ; ++j) {
-        const int i = t + NT * m + kPartials * j;
-        if (i < V && q[m][j] >= tau) {
-          const unsigned pos = atomicAdd(cn, 1u);
-          if (pos < kCandCap) sm.cand[pos] = cand_key(q[m][j], (uint32_t)i);
+      __threadfence_block();
+      if (atomicAdd(&sm.stage_done[s], 1u) == kFastW - 1) {
+        // every warp has added its candidates: the row's count is final
+        H.cnt = (int)sm.cand_n[s];
+        sm.cand_n[s] = 0;
+        sm.stage_done[s] = 0;
+        const int nrow = row + stages * (int)gridDim.x;
+        if (nrow < a.N) {
+          fence_proxy_async();
+          issue_row<ESZ>(a, nrow, dsm + (size_t)s * span, &sm.mbar[s], pol);
         }
       }
-    __syncthreads();
-    unsigned C = *cn;
-    if (C > kSortMax) {
-      // Too many at the threshold (ties): the k-th largest key exactly, by
-      // bisection on the 64-bit (value, id) key; then exactly the k keys above it.
-      unsigned long long P = 0;
-      for (int b = 63; b >= 0; --b) {
-        const unsigned long long trial = P | (1ull << b);
-        int c = 0;
-#pragma unroll
-        for (int m = 0; m < PP; ++m)
-#pragma unroll
-          for (int j = 0; j < JJ; ++j) {
-            const int i = t + NT * m + kPartials * j;
-            c += (i < V && cand_key(q[m][j], (uint32_t)i) >= trial) ? 1 : 0;
-          }
-        c = __reduce_add_sync(kFull, c);
-        if (lane == 0) sm.red_cnt[b & 1][w] = c;
-        __syncthreads();
-        int tot = 0;
-#pragma unroll
-        for (int i = 0; i < kFastW; ++i) tot += sm.red_cnt[b & 1][i];
-        if (tot >= rp.k) P = trial;
-      }
-      if (t == 0) *cn = 0;
-      __syncthreads();
-#pragma unroll
-      for (int m = 0; m < PP; ++m)
-#pragma unroll
-        for (int j = 0; j < JJ; ++j) {
-          const int i = t + NT * m + kPartials * j;
-          if (i < V) {
-            const unsigned long long key = cand_key(q[m][j], (uint32_t)i);
-            if (key >= P) sm.cand[atomicAdd(cn, 1u)] = key;
-          }
-        }
-      __syncthreads();
-      C = (unsigned)rp.k;
-    }
-    if (w == 0) {
-      warp_sort_any(sm.cand, (int)C, lane);
-      sample_tail(a, row, sm.cand, sm.scr, rp.k, lse, rp.p, lane);
     }
   }
   if (failed) {
@@ -600,6 +618,193 @@ __global__ void __launch_bounds__(kFastThreads) sample_fast_kernel(const KArgs a
   }
 }
 
+// ---- select kernel (K2): one warp per row ----
+
+constexpr int kSelWarps = 8;
+constexpr int kSelThreads = 32 * kSelWarps;
+
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+  const unsigned lo = __shfl_xor_sync(kFull, (unsigned)v, m);
+  const unsigned hi = __shfl_xor_sync(kFull, (unsigned)(v >> 32), m);
+  return ((unsigned long long)hi << 32) | lo;
+}
+
+// Compare-exchange of elements e (in x) and e + stride (in y) of one lane.
+__device__ __forceinline__ void inreg_exchange(unsigned long long &x, unsigned long long &y, int e,
+                                               int size) {
+  const bool desc = (e & size) == 0;
+  const bool swap = desc ? (x < y) : (x > y);
+  const unsigned long long a = x;
+  x = swap ? y : x;
+  y = swap ? a : y;
+}
+
+// Bitonic sort of 32 * S keys held as v[s] = element lane + 32 s, descending.
+// The stage loops stay rolled (small code); only the S keys of a lane unroll.
+template <int S>
+__device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int lane) {
+  constexpr int n = 32 * S;
+#pragma unroll 1
+  for (int size = 2; size <= n; size <<= 1) {
+#pragma unroll 1
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride < 32) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+          const unsigned long long o = shfl_xor_u64(v[s], stride);
+          const bool desc = ((lane + 32 * s) & size) == 0;
+          const bool keep_max = ((lane & stride) == 0) == desc;
+          const unsigned long long mx = v[s] > o ? v[s] : o, mn = v[s] > o ? o : v[s];
+          v[s] = keep_max ? mx : mn;
+        }
+      } else if constexpr (S >= 2) {
+        // partners in the same lane: register s and s ^ (stride / 32)
+        if (stride == 32) {
+#pragma unroll
+          for (int s = 0; s < S; s += 2) inreg_exchange(v[s], v[s + 1], lane + 32 * s, size);
+        } else if constexpr (S >= 4) {
+#pragma unroll
+          for (int s = 0; s < S; ++s)
+            if ((s & 2) == 0) inreg_exchange(v[s], v[s + 2], lane + 32 * s, size);
+        }
+      }
+    }
+  }
+}
+
+// Sort the row's C <= 32 S candidates (the first 64 staged in cs, the rest in
+// the slab) with the warp and store the first k keys, in rank order, into sk.
+template <int S>
+__device__ __forceinline__ void sort_cands(const unsigned long long *cs, const RowCands &Cs,
+                                           int C, int k, unsigned long long *sk, int lane) {
+  unsigned long long v[S];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const int e = lane + 32 * s;
+    v[s] = e < C ? (e < 64 ? cs[e] : Cs.cand[e]) : 0ull;
+  }
+  warp_sort_desc<S>(v, lane);
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+    if (lane + 32 * s < k) sk[lane + 32 * s] = v[s];
+}
+
+// More than 128 candidates: the k largest taken one at a time (two warp reduxes
+// per rank), into sk in rank order.
+__device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k,
+                                             unsigned long long *sk, int lane) {
+  unsigned long long v[8], best = 0ull;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const int e = lane + 32 * s;
+    v[s] = e < C ? Cs.cand[e] : 0ull;
+    best = v[s] > best ? v[s] : best;
+  }
+  for (int r = 0; r < k; ++r) {
+    const unsigned mh = __reduce_max_sync(kFull, (unsigned)(best >> 32));
+    const unsigned ml =
+        __reduce_max_sync(kFull, (unsigned)(best >> 32) == mh ? (unsigned)best : 0u);
+    const unsigned long long wk = ((unsigned long long)mh << 32) | ml;
+    if (best == wk) {
+      unsigned long long nb = 0ull;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (v[s] == wk) v[s] = 0ull;
+        nb = v[s] > nb ? v[s] : nb;
+      }
+      best = nb;
+    }
+    if (lane == 0) sk[r] = wk;
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_prev() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// A row's header and its first 64 candidate slots, staged by cp.async.
+struct alignas(16) SelStage {
+  RowHead head;
+  unsigned long long cand[64];
+};
+
+constexpr int kHeadChunks = (int)(sizeof(RowHead) / 16);
+static_assert(sizeof(RowHead) % 16 == 0 && kHeadChunks <= 32, "RowHead is copied in 16-byte chunks");
+
+__device__ __forceinline__ void stage_row(const RowHead *heads, const RowCands *cands, int row,
+                                          SelStage &st, int lane) {
+  if (lane < kHeadChunks)
+    cp_async16(reinterpret_cast<char *>(&st.head) + 16 * lane,
+               reinterpret_cast<const char *>(heads + row) + 16 * lane);
+  cp_async16(reinterpret_cast<char *>(st.cand) + 16 * lane,
+             reinterpret_cast<const char *>(cands + row) + 16 * lane);
+}
+
+__global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KArgs a,
+                                                                        const RowHead *heads,
+                                                                        const RowCands *cands) {
+  __shared__ __align__(16) float scr_all[kSelWarps][kFastMaxK + 4];
+  __shared__ unsigned long long sk_all[kSelWarps][kFastMaxK];
+  __shared__ SelStage stg_all[kSelWarps][2];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int gw = blockIdx.x * kSelWarps + w, nw = gridDim.x * kSelWarps;
+  unsigned long long *sk = sk_all[w];
+  int row = gw, b = 0;
+  RawP raw;
+  if (row < a.N) {
+    stage_row(heads, cands, row, stg_all[w][0], lane);
+    raw = load_raw(a, row);
+  }
+  cp_async_commit();
+  for (; row < a.N; row += nw, b ^= 1) {
+    // the next row's header and candidates are copied while this row is sampled
+    const int nrow = row + nw;
+    RawP rawn;
+    __syncwarp();
+    if (nrow < a.N) {
+      stage_row(heads, cands, nrow, stg_all[w][b ^ 1], lane);
+      rawn = load_raw(a, nrow);
+    }
+    cp_async_commit();
+    cp_async_wait_prev();
+    __syncwarp();
+    const SelStage &st = stg_all[w][b];
+    if (!st.head.done) {
+      RowP rp;
+      resolve(a, raw, rp);  // valid: the stats kernel flagged every other row
+      const int C = st.head.cnt;
+      unsigned long long S = 0;
+#pragma unroll
+      for (int i = 0; i < kFastW; ++i) S += st.head.sum[i];
+      if (C > kCandCap) {  // more candidates than the list holds (ties): the wide kernel's exact path
+        if (lane == 0) defer_row(a, row);
+      } else {
+        const RowCands &Cs = cands[row];
+        const float lse = __fadd_rn(st.head.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
+        const uint2 key = a.noise == D3S_NOISE_SEEDS ? seed_subkey(raw.seed) : a.key;
+        if (C <= 32)
+          sort_cands<1>(st.cand, Cs, C, rp.k, sk, lane);
+        else if (C <= 64)
+          sort_cands<2>(st.cand, Cs, C, rp.k, sk, lane);
+        else if (C <= 128)
+          sort_cands<4>(st.cand, Cs, C, rp.k, sk, lane);
+        else
+          select_cands(Cs, C, rp.k, sk, lane);
+        __syncwarp();
+        sample_tail(a, row, key, sk, scr_all[w], rp.k, lse, rp.p, lane);
+      }
+    }
+    raw = rawn;
+  }
+}
+
 // ---- wide kernel ----
 
 template <bool BF16>
@@ -610,9 +815,9 @@ __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a
   __shared__ unsigned long long red_sum[kWideWarps];
   __shared__ int red_cnt[2][kWideWarps];
   __shared__ unsigned gather_n;
-  int kp_cap = 1;
+  int kp_cap = 2;
   while (kp_cap < kcap) kp_cap <<= 1;
-  float *scr = reinterpret_cast<float *>(keys + kp_cap);
+  float *scr = reinterpret_cast<float *>(keys + kp_cap);  // 16-byte aligned: kp_cap is even
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int V = a.V;
   const unsigned nrows =
@@ -691,7 +896,7 @@ __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a
         __syncthreads();
       }
     }
-    if (w == 0) sample_tail(a, row, keys, scr, k, lse, rp.p, lane);
+    if (w == 0) sample_tail(a, row, row_key(a, row), keys, scr, k, lse, rp.p, lane);
     __syncthreads();
   }
   if (use_list) {
@@ -744,7 +949,7 @@ __global__ void div_check_kernel(const float *Ts, int nT, uint64_t lo, uint64_t 
          f += (uint64_t)gridDim.x * blockDim.x) {
       const float x = __uint_as_float((uint32_t)(lo + f * step));
       const float ax = fabsf(x);
-      if (!(ax >= 0x1p-60f && ax <= 0x1p60f)) continue;
+      if (!(ax >= 0x1p-100f && ax <= 0x1p60f)) continue;
       const float q = div_rows(x, rT, mT), ref = __fdiv_rn(x, T);
       if (__float_as_uint(q) != __float_as_uint(ref)) {
         ++local;
@@ -758,22 +963,28 @@ __global__ void div_check_kernel(const float *Ts, int nT, uint64_t lo, uint64_t 
 
 // ---- launch helpers ----
 
-using FastFn = void (*)(const KArgs, int, int);
+using StatFn = void (*)(const KArgs, RowHead *, RowCands *, int, int);
 
-template <bool BF16>
-FastFn pick_fast(int J) {
+template <bool BF16, bool EXACT>
+StatFn pick_stats_e(int J) {
   switch (J) {
-    case 1: return sample_fast_kernel<1, BF16>;
-    case 2: return sample_fast_kernel<2, BF16>;
-    case 4: return sample_fast_kernel<4, BF16>;
-    case 8: return sample_fast_kernel<8, BF16>;
-    case 12: return sample_fast_kernel<12, BF16>;
-    case 16: return sample_fast_kernel<16, BF16>;
-    case 17: return sample_fast_kernel<17, BF16>;
-    case 24: return sample_fast_kernel<24, BF16>;
-    case 32: return sample_fast_kernel<32, BF16>;
+    case 1: return sample_stats_kernel<1, BF16, EXACT>;
+    case 2: return sample_stats_kernel<2, BF16, EXACT>;
+    case 4: return sample_stats_kernel<4, BF16, EXACT>;
+    case 8: return sample_stats_kernel<8, BF16, EXACT>;
+    case 12: return sample_stats_kernel<12, BF16, EXACT>;
+    case 16: return sample_stats_kernel<16, BF16, EXACT>;
+    case 17: return sample_stats_kernel<17, BF16, EXACT>;
+    case 24: return sample_stats_kernel<24, BF16, EXACT>;
+    case 32: return sample_stats_kernel<32, BF16, EXACT>;
     default: return nullptr;
   }
+}
+
+template <bool BF16>
+StatFn pick_stats(int J, int V) {
+  return J == (V + kPartials - 1) / kPartials ? pick_stats_e<BF16, true>(J)
+                                              : pick_stats_e<BF16, false>(J);
 }
 
 int pick_J(int V) {
@@ -805,9 +1016,9 @@ int occupancy(const void *fn, int threads, size_t smem) {
 }
 
 size_t wide_smem(int kcap) {
-  int kp = 1;
+  int kp = 2;
   while (kp < kcap) kp <<= 1;
-  return (size_t)kp * sizeof(unsigned long long) + (size_t)kcap * sizeof(float);
+  return (size_t)kp * sizeof(unsigned long long) + (size_t)(kcap + 4) * sizeof(float);
 }
 
 template <bool BF16>
@@ -825,14 +1036,15 @@ int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
 }
 
+// The fast path: stats (K1) -> select (K2) -> wide kernel for the rows handed on.
 template <bool BF16>
-int launch_fast(const KArgs &a, int J, cudaStream_t st) {
+int launch_fast(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStream_t st) {
   constexpr int esz = BF16 ? 2 : 4;
   const int span = ((a.V * esz + 15) / 16) * 16 + 16;
   int stages = BF16 ? 3 : 2;
   while (stages > 2 && (size_t)stages * span > 64 * 1024) --stages;
   const size_t smem = (size_t)stages * span;
-  FastFn fn = pick_fast<BF16>(J);
+  StatFn fn = pick_stats<BF16>(J, a.V);
   if (!fn) return D3S_ERR_ARG;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
@@ -840,8 +1052,13 @@ int launch_fast(const KArgs &a, int J, cudaStream_t st) {
   const int sms = device_sms();
   if (sms <= 0) return D3S_ERR_CUDA;
   const int grid = std::max(1, std::min(a.N, sms * occupancy((const void *)fn, kFastThreads, smem)));
-  fn<<<grid, kFastThreads, smem, st>>>(a, stages, span);
-  return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+  fn<<<grid, kFastThreads, smem, st>>>(a, sc.heads, sc.cands, stages, span);
+  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  const int sel_occ = occupancy((const void *)sample_select_kernel, kSelThreads, 0);
+  const int sel_grid = std::max(1, std::min((a.N + kSelWarps - 1) / kSelWarps, sms * sel_occ));
+  sample_select_kernel<<<sel_grid, kSelThreads, 0, st>>>(a, sc.heads, sc.cands);
+  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  return launch_wide<BF16>(a, 1, wide_kcap, st);
 }
 
 template <bool BF16>
@@ -851,11 +1068,9 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
   const int kscalar = std::min(a.top_k, a.V);
   if (J == 0 || (scalar_k && kscalar > kFastMaxK))
     return launch_wide<BF16>(a, 0, scalar_k ? kscalar : D3S_MAX_K, st);
-  if (!scalar_k && (!s.deferred || !s.counters || s.capacity < a.N)) return D3S_ERR_ARG;
-  const int rc = launch_fast<BF16>(a, J, st);
-  if (rc != D3S_OK) return rc;
-  if (!scalar_k) return launch_wide<BF16>(a, 1, D3S_MAX_K, st);
-  return D3S_OK;
+  if (!s.deferred || !s.counters || s.capacity < a.N || !s.heads || s.rec_capacity < a.N)
+    return D3S_ERR_ARG;
+  return launch_fast<BF16>(a, s, J, scalar_k ? kscalar : D3S_MAX_K, st);
 }
 
 }  // namespace

@@ -39,7 +39,22 @@ struct KArgs {
   int32_t *error;        // set to 1 when a bounded wait gives up
 };
 
-// Device scratch a launch needs: `deferred` holds N int32; counters holds 3
+// Per-row results the stats kernel passes to the select kernel. The header
+// (dense, one per row): the row max in q, the candidate count and the four
+// warps' 2^-46 fixed-point partial sums. The candidates, as (value, id) keys in
+// no particular order, live in a separate slab.
+struct alignas(16) RowHead {
+  float gmax;
+  int done;  // 1: the stats kernel already wrote the row's result (or handed it on)
+  int cnt;   // candidates (the first min(cnt, 256) are stored)
+  int pad;
+  unsigned long long sum[4];
+};
+struct alignas(16) RowCands {
+  unsigned long long cand[256];
+};
+
+// Device scratch a launch needs: N RowHeads and RowCands, `deferred` N int32; counters holds 3
 // uint32 that must be zero before the first launch: the hand-off count and the
 // wide kernel's completion count (the wide kernel re-zeroes both), and the
 // error word (cleared by the host when it reads it).
@@ -47,6 +62,9 @@ struct Scratch {
   int32_t *deferred = nullptr;
   uint32_t *counters = nullptr;
   int64_t capacity = 0;
+  RowHead *heads = nullptr;  // one per row of the largest request so far
+  RowCands *cands = nullptr;
+  int64_t rec_capacity = 0;
 };
 
 // Launch the sampler for one request. Validates sizes; returns D3S_* status.

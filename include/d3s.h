@@ -89,13 +89,15 @@ D3S_API int d3s_next_key(d3s_key *state, d3s_key *sub);
 
 /* ---- context ---- */
 
-/* A context owns the device id, scratch for the rows that need the wide
- * selection path, and staging buffers for the host-pointer entry points. */
+/* A context owns the device id, the kernels' device scratch (per-row records
+ * passed between the streaming and the selection kernel, the hand-off list of
+ * rows for the wide path) and staging buffers for the host-pointer entry points. */
 D3S_API int d3s_ctx_create(int device, d3s_ctx **out);
 D3S_API void d3s_ctx_destroy(d3s_ctx *ctx);
-/* Pre-size the scratch for requests of up to max_rows rows with per-row top_k
- * (d3s_request.top_k_rows). d3s_sample grows it on demand with cudaMalloc,
- * which a CUDA graph capture cannot contain: reserve before capturing. */
+/* Pre-size the context's device scratch (about 2.1 KB of row records plus a
+ * 4-byte hand-off slot per row) for requests of up to max_rows rows.
+ * d3s_sample grows it on demand with cudaMalloc, which a CUDA graph capture
+ * cannot contain: reserve before capturing. */
 D3S_API int d3s_ctx_reserve(d3s_ctx *ctx, int64_t max_rows);
 
 /* ---- the reference's internal API (src/model.h:169-176) ---- */
@@ -149,13 +151,12 @@ D3S_API int d3s_sample(d3s_ctx *ctx, const d3s_request *req, void *stream);
 D3S_API int d3s_ctx_check(d3s_ctx *ctx);
 
 /* Test hooks (no counterpart in the reference): y_dev = f(x_dev) with the
- * kernels' own arithmetic; op 0 = exp, 1 = log, 2 = the full-row-sum term (exp,
- * or 0 when its 2^n scale is subnormal), 3 = x / param by the per-row
- * reciprocal path. */
+ * kernels' own arithmetic; op 0 = exp, 1 = log, 2 = the full-row-sum term
+ * exp(max(x, -87)), 3 = x / param by the per-row reciprocal path. */
 D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
                            float param, void *stream);
-/* Counts float bit patterns x in [lo, hi) (step `step`) inside the reciprocal
- * path's range whose quotient x / T differs from the IEEE quotient, for each of
+/* Counts float bit patterns x in [lo, hi) (step `step`) with |x| in
+ * [2^-100, 2^60], the reciprocal path's exact range, whose quotient x / T differs from the IEEE quotient, for each of
  * T_dev[nT]; adds to *bad_dev (device), last failing (x, T) in example_dev[2]. */
 D3S_API int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64_t lo,
                                 uint64_t hi, uint64_t step, unsigned long long *bad_dev,

@@ -185,17 +185,13 @@ float d3o_log(float x) {
   return fmaf(ef, D3_LN2_HI, fmaf(ef, D3_LN2_LO, L));
 }
 
-/* A term of the full-row sum: exp(d) for d = q - max <= 0, except that a term
- * whose scale 2^n (n = the nearest integer to d log2 e, as d3o_exp computes it)
- * is below the normal range, i.e. n <= -127 and exp(d) < 2^-126, is taken as 0.
- * Such terms are far below the 2^-46 resolution of the fixed-point sum. NaN
- * stays NaN (it marks a non-finite row); -inf gives 0. */
+/* A term of the full-row sum, d = q - max <= 0: exp(max(d, -87)). Below -87
+ * the term (< 2^-125) is far under the 2^-46 resolution of the fixed-point
+ * sum; the floor keeps exp's 2^n scale in the normal range. NaN stays NaN (it
+ * marks a non-finite row); -inf gives exp(-87). */
 static float d3o_exp_term(float d) {
   if (d != d) return d;
-  if (d < -110.0f) d = -110.0f;
-  float t = fmaf(d, D3_L2E, D3_SHIFTER);
-  int32_t n = (int32_t)(f2u(t) - f2u(D3_SHIFTER));
-  if (n <= -127) return 0.0f;
+  if (d < -87.0f) d = -87.0f;
   return d3o_exp(d);
 }
 

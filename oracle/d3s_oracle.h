@@ -31,7 +31,8 @@
  *   - the full-row sum of exp(q - max) is taken as 256 strided partials
  *     (partial p sums elements p, p+256, ... in order, in float), each partial
  *     truncated to a 2^-46 fixed-point uint64 and the partials added exactly.
- *     A term whose 2^n scale is subnormal (exp(q - max) < 2^-126) counts as 0.
+ *     Each term is exp(max(q - max, -87)): below -87 a term is far under the
+ *     fixed point's resolution, and the floor keeps exp's scale normal.
  *   - the row maximum ignores the sign of zero (-0 and +0 compare equal, as in
  *     every comparison of the path); top-k order is (value desc, id asc).
  */
@@ -65,7 +66,7 @@ float d3o_exp(float x);
 float d3o_log(float x);
 void d3o_exp_array(const float *x, float *y, int64_t n);
 void d3o_log_array(const float *x, float *y, int64_t n);
-/* the full-row-sum term: exp(d), or 0 when its 2^n scale is subnormal */
+/* the full-row-sum term: exp(max(d, -87)) */
 void d3o_term_array(const float *x, float *y, int64_t n);
 
 /* ---- sampler ---- */

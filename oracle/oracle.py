@@ -195,7 +195,7 @@ def log(x: np.ndarray) -> np.ndarray:
 
 
 def exp_term(x: np.ndarray) -> np.ndarray:
-    """The full-row-sum term (exp, or 0 when its 2^n scale is subnormal)."""
+    """The full-row-sum term exp(max(d, -87))."""
     x = np.ascontiguousarray(x, np.float32)
     y = np.empty_like(x)
     lib().d3o_term_array(_p(x, _f32p), _p(y, _f32p), x.size)

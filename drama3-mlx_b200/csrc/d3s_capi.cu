@@ -198,6 +198,8 @@ int take_subkey(d3s_key *state, d3s_key *sub) {
 
 }  // namespace
 
+int d3s::set_error(int code, const char *msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 int d3s_version(void) { return D3S_VERSION; }

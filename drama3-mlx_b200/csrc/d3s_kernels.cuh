@@ -70,6 +70,9 @@ struct Scratch {
 // Launch the sampler for one request. Validates sizes; returns D3S_* status.
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t stream);
 
+// Record an error message for d3s_last_error() on this thread; returns code.
+int set_error(int code, const char *msg);
+
 // Draw u [rows, k] = uniform(key, rows * k) (sample_noise).
 int launch_uniform(uint2 key, int rows, int k, float *u, cudaStream_t stream);
 

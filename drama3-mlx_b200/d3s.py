@@ -39,8 +39,9 @@ MAX_K = 16384
 EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split", "d3s_seed",
            "d3s_next_key", "d3s_ctx_create", "d3s_ctx_destroy", "d3s_ctx_reserve",
            "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
-           "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3_sample",
-           "d3s_last_status")
+           "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3s_sample_rows_static",
+           "d3_sample", "d3s_last_status")
+STATIC_MAX_ROWS = 4096
 
 
 class D3SError(RuntimeError):
@@ -110,6 +111,7 @@ def lib() -> ctypes.CDLL:
         L.d3s_debug_math.argtypes = [vp, i32, vp, vp, i64, f32, vp]
         L.d3s_debug_div_check.argtypes = [vp, vp, i32, u64, u64, u64, vp, vp, vp]
         L.d3s_ctx_check.argtypes = [vp]
+        L.d3s_sample_rows_static.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp]
         L.d3_sample.argtypes = [ctypes.POINTER(ctypes.c_float), i32, i32, f32, i32, f32,
                                 ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_int32)]
         L.d3_sample.restype = None
@@ -146,6 +148,14 @@ def next_key(state: Key | None = None) -> Key:
     sub = Key()
     _check(lib().d3s_next_key(ctypes.byref(state) if state is not None else None, ctypes.byref(sub)))
     return sub
+
+
+def sample_rows_static(logits, ids, temperature, top_p, top_k, seeds, stream=None) -> None:
+    """d3s_sample_rows_static on CUDA tensors (all per-row arrays required)."""
+    N, V = logits.shape
+    _check(lib().d3s_sample_rows_static(_ptr(logits), _dtype_code(logits), N, V, logits.stride(0),
+                                        _ptr(temperature), _ptr(top_p), _ptr(top_k), _ptr(seeds),
+                                        _ptr(ids), _stream_ptr(stream)))
 
 
 # ---- the reference's test entry point ----

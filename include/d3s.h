@@ -162,6 +162,29 @@ D3S_API int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64
                                 uint64_t hi, uint64_t step, unsigned long long *bad_dev,
                                 float *example_dev, void *stream);
 
+/* ---- batched sampling without allocation ---- */
+
+/* Rows a d3s_sample_rows_static call may hold (about 8.6 MB of device scratch
+ * that every GPU loading this library keeps until the process exits). */
+#define D3S_STATIC_MAX_ROWS 4096
+
+/* No counterpart in the reference. For callers that cannot allocate device
+ * memory while they sample: a serving engine that budgets every device byte
+ * up front, a real-time audio thread that cannot wait on cudaMalloc's implicit
+ * device synchronisation, code running inside someone else's stream capture.
+ * Same results as d3s_sample with D3S_NOISE_SEEDS and per-row temperature,
+ * top_p and top_k (all device arrays of N, as are the logits and ids); no
+ * context is needed. Its scratch is one fixed array in the library shared by
+ * every call: N above D3S_STATIC_MAX_ROWS is rejected (D3S_ERR_UNSUPPORTED),
+ * and two calls whose kernels overlap on the GPU (different streams without an
+ * ordering between them) race on it. The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before capturing a CUDA graph. Nothing is allocated, on any call. */
+D3S_API int d3s_sample_rows_static(const void *logits_dev, int dtype, int N, int V, int64_t ld,
+                                   const float *temperature_dev, const float *top_p_dev,
+                                   const int32_t *top_k_dev, const uint64_t *seeds_dev,
+                                   int32_t *ids_dev, void *stream);
+
 /* ---- the reference's test C-ABI (src/testapi.c:155-166) ---- */
 
 /* Host logits [N, V] f32 -> host ids [N]: seeds the global key with `seed`,

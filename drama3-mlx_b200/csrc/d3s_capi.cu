@@ -133,6 +133,11 @@ int check_request(const d3s_request *r) {
     case D3S_NOISE_SEEDS:
       if (r->N > 0 && !r->seeds) return fail(D3S_ERR_ARG, "null seeds");
       break;
+    case D3S_NOISE_KEYS:
+      if (r->N > 0 && !r->keys) return fail(D3S_ERR_ARG, "null keys");
+      if (((uintptr_t)r->keys & 7) != 0) return fail(D3S_ERR_ARG, "keys must be 8-byte aligned");
+      if (r->ld_keys < 0) return fail(D3S_ERR_ARG, "ld_keys < 0");
+      break;
     case D3S_NOISE_GIVEN:
       if (r->N > 0 && !r->u) return fail(D3S_ERR_ARG, "null u");
       if (r->top_k_rows) return fail(D3S_ERR_ARG, "given noise needs one top_k for the batch");
@@ -172,6 +177,10 @@ d3s::KArgs to_kargs(const d3s_request *r, const d3s_ctx *ctx) {
   a.probs = r->probs;
   a.topk_ids = r->topk_ids;
   a.ld_out = r->ld_out;
+  a.keys = reinterpret_cast<const uint2 *>(r->keys);
+  a.ld_keys = r->ld_keys > 0 ? r->ld_keys : 1;
+  a.finite = r->finite;
+  a.row_period = 0;
   a.deferred = ctx->scratch.deferred;
   a.deferred_n = ctx->scratch.counters;
   a.wide_done = ctx->scratch.counters ? ctx->scratch.counters + 1 : nullptr;

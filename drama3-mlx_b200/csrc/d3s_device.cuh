@@ -11,18 +11,21 @@
 
 namespace d3s {
 
-// Float roundings of log2(e), ln(2) (high part and the remainder), the Taylor
-// coefficients 1/k! and the atanh-series coefficients 1/(2j+1).
+// Float roundings of log2(e), ln(2) (high part and the remainder), the
+// coefficients of exp's polynomial on [-ln2/2, ln2/2] (p(r) = 1 + r + r^2 q(r)
+// with q of degree 4, minimax for the relative error of p, derived by a
+// linear program over a dense grid and rounded to float) and the atanh-series
+// coefficients 1/(2j+1).
 constexpr float kL2E = 0x1.715476p+0f;
 constexpr float kLn2Hi = 0x1.62e430p-1f;
 constexpr float kLn2Lo = -0x1.05c610p-29f;
 constexpr float kShifter = 0x1.8p23f;  // adding it rounds to an integer in the low bits
 constexpr uint32_t kShifterBits = 0x4B400000u;
-constexpr float kInvF7 = 0x1.a01a02p-13f;
-constexpr float kInvF6 = 0x1.6c16c2p-10f;
-constexpr float kInvF5 = 0x1.111112p-7f;
-constexpr float kInvF4 = 0x1.555556p-5f;
-constexpr float kInvF3 = 0x1.555556p-3f;
+constexpr float kE6 = 0x1.69d528p-10f;
+constexpr float kE5 = 0x1.126946p-7f;
+constexpr float kE4 = 0x1.55596cp-5f;
+constexpr float kE3 = 0x1.55544p-3f;
+constexpr float kE2 = 0x1.fffffcp-2f;
 constexpr float kInv13 = 0x1.3b13b2p-4f;
 constexpr float kInv11 = 0x1.745d18p-4f;
 constexpr float kInv9 = 0x1.c71c72p-4f;
@@ -54,7 +57,7 @@ __device__ __forceinline__ float warp_max(float a) {
 }
 
 // exp over the whole float range: Cody-Waite reduction against a two-float
-// ln 2, degree-7 Taylor polynomial in Horner form, exact scaling by 2^n (two
+// ln 2, the degree-6 polynomial in Horner form, exact scaling by 2^n (two
 // steps outside the normal range so a subnormal result rounds once).
 __device__ __forceinline__ float exp_full(float x) {
   if (x < -104.0f) return 0.0f;
@@ -62,14 +65,13 @@ __device__ __forceinline__ float exp_full(float x) {
   float t = __fmaf_rn(x, kL2E, kShifter);
   float nf = __fsub_rn(t, kShifter);
   int n = (int)(__float_as_uint(t) - kShifterBits);
-  float r = __fmaf_rn(-nf, kLn2Hi, x);
-  r = __fmaf_rn(-nf, kLn2Lo, r);
-  float p = kInvF7;
-  p = __fmaf_rn(p, r, kInvF6);
-  p = __fmaf_rn(p, r, kInvF5);
-  p = __fmaf_rn(p, r, kInvF4);
-  p = __fmaf_rn(p, r, kInvF3);
-  p = __fmaf_rn(p, r, 0.5f);
+  float r = __fmaf_rn(nf, -kLn2Hi, x);
+  r = __fmaf_rn(nf, -kLn2Lo, r);
+  float p = kE6;
+  p = __fmaf_rn(p, r, kE5);
+  p = __fmaf_rn(p, r, kE4);
+  p = __fmaf_rn(p, r, kE3);
+  p = __fmaf_rn(p, r, kE2);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
   int n2 = n < -126 ? -64 : (n > 127 ? 1 : 0);
@@ -78,60 +80,57 @@ __device__ __forceinline__ float exp_full(float x) {
   return __fmul_rn(__fmul_rn(p, s1), s2);
 }
 
-// One term of the full-row sum for d = q - max in [-inf, 0] (never NaN):
-// exp(max(d, -87)). Below -87 the term (< 2^-125) is far under the 2^-46
-// resolution of the fixed-point sum; the clamp keeps the 2^n scale normal
-// (n >= -126), so the scale is (n + 127) << 23 = (t's bits << 23) + (127 << 23)
-// (t = 1.5 * 2^23 + n, whose bits are 0x4B400000 + n; 0x4B400000 << 23 wraps
-// to 0) and the result p * 2^n rounds once, as exp_full's does.
-// (n + 127) << 23 from t's bits, as one integer multiply-add.
-__device__ __forceinline__ float term_scale(float t) {
+// p * 2^n for p in [0.7, 1.42] and n >= -124, as integers: t = 1.5 * 2^23 + n has
+// bits 0x4B400000 + n, and (0x4B400000 << 23) wraps to 0, so bits(p) + (t's bits
+// << 23) adds n to p's exponent. The result is normal, so this is exactly the
+// rounded product p * 2^n.
+__device__ __forceinline__ float scale_pow2(float p, float t) {
   unsigned r;
-  asm("mad.lo.u32 %0, %1, 8388608, 1065353216;" : "=r"(r) : "r"(__float_as_uint(t)));
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r) : "r"(__float_as_uint(t)), "r"(__float_as_uint(p)));
   return __uint_as_float(r);
 }
 
-constexpr float kTermFloor = -87.0f;
+// One term of the full-row sum for d = q - max in [-inf, 0] (never NaN):
+// exp(max(d, -86)). Below -86 a term (< 2^-124) is far under the 2^-46
+// resolution of the fixed-point sum; the floor keeps n >= -124, so the result
+// is normal and equals exp_full's.
+constexpr float kTermFloor = -86.0f;
 __device__ __forceinline__ float exp_term(float d) {
   d = fmaxf(d, kTermFloor);
   float t = __fmaf_rn(d, kL2E, kShifter);
   float nf = __fsub_rn(t, kShifter);
-  float r = __fmaf_rn(-nf, kLn2Hi, d);
-  r = __fmaf_rn(-nf, kLn2Lo, r);
-  float p = kInvF7;
-  p = __fmaf_rn(p, r, kInvF6);
-  p = __fmaf_rn(p, r, kInvF5);
-  p = __fmaf_rn(p, r, kInvF4);
-  p = __fmaf_rn(p, r, kInvF3);
-  p = __fmaf_rn(p, r, 0.5f);
+  float r = __fmaf_rn(nf, -kLn2Hi, d);
+  r = __fmaf_rn(nf, -kLn2Lo, r);
+  float p = kE6;
+  p = __fmaf_rn(p, r, kE5);
+  p = __fmaf_rn(p, r, kE4);
+  p = __fmaf_rn(p, r, kE3);
+  p = __fmaf_rn(p, r, kE2);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  return __fmul_rn(p, term_scale(t));
+  return scale_pow2(p, t);
 }
 
 // Two terms at once on the packed fp32x2 pipe (sm_100a); same roundings as
-// exp_term, element by element. CLAMP = false when the caller knows d >= -87.
+// exp_term, element by element. CLAMP = false when the caller knows d >= -86.
 template <bool CLAMP>
 __device__ __forceinline__ float2 exp_term2(float2 d) {
   if (CLAMP) {
     d.x = fmaxf(d.x, kTermFloor);
     d.y = fmaxf(d.y, kTermFloor);
   }
-  const float2 l2e = make_float2(kL2E, kL2E), sh = make_float2(kShifter, kShifter);
-  float2 t = __ffma2_rn(d, l2e, sh);
+  float2 t = __ffma2_rn(d, make_float2(kL2E, kL2E), make_float2(kShifter, kShifter));
   float2 nf = __fadd2_rn(t, make_float2(-kShifter, -kShifter));
-  float2 mnf = make_float2(-nf.x, -nf.y);
-  float2 r = __ffma2_rn(mnf, make_float2(kLn2Hi, kLn2Hi), d);
-  r = __ffma2_rn(mnf, make_float2(kLn2Lo, kLn2Lo), r);
-  float2 p = make_float2(kInvF7, kInvF7);
-  p = __ffma2_rn(p, r, make_float2(kInvF6, kInvF6));
-  p = __ffma2_rn(p, r, make_float2(kInvF5, kInvF5));
-  p = __ffma2_rn(p, r, make_float2(kInvF4, kInvF4));
-  p = __ffma2_rn(p, r, make_float2(kInvF3, kInvF3));
-  p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
+  float2 r = __ffma2_rn(nf, make_float2(-kLn2Hi, -kLn2Hi), d);
+  r = __ffma2_rn(nf, make_float2(-kLn2Lo, -kLn2Lo), r);
+  float2 p = make_float2(kE6, kE6);
+  p = __ffma2_rn(p, r, make_float2(kE5, kE5));
+  p = __ffma2_rn(p, r, make_float2(kE4, kE4));
+  p = __ffma2_rn(p, r, make_float2(kE3, kE3));
+  p = __ffma2_rn(p, r, make_float2(kE2, kE2));
   p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
   p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
-  return __fmul2_rn(p, make_float2(term_scale(t.x), term_scale(t.y)));
+  return make_float2(scale_pow2(p.x, t.x), scale_pow2(p.y, t.y));
 }
 
 // log: x = 2^e m, m in (sqrt2/2, sqrt2], s = (m-1)/(m+1), log m = 2 atanh(s)

@@ -106,9 +106,15 @@ __device__ __forceinline__ float lds_x(const unsigned char *base, int i) {
     return reinterpret_cast<const float *>(base)[i];
 }
 
+// The logits row a (virtual) row reads: draws that share logits (the main and
+// the retry draw of a frame) are rows r and r + row_period of one request.
+__device__ __forceinline__ int64_t phys_row(const KArgs &a, int row) {
+  return a.row_period > 0 ? (int64_t)(row % a.row_period) : (int64_t)row;
+}
+
 template <bool BF16>
 __device__ __forceinline__ const void *row_base(const KArgs &a, int row) {
-  const int64_t off = (int64_t)row * a.ld;
+  const int64_t off = phys_row(a, row) * a.ld;
   if constexpr (BF16)
     return reinterpret_cast<const unsigned short *>(a.logits) + off;
   else
@@ -142,7 +148,9 @@ __device__ __forceinline__ void flag_row(const KArgs &a, int row, int code) {
 }
 
 __device__ __forceinline__ uint2 row_key(const KArgs &a, int row) {
-  return a.noise == D3S_NOISE_SEEDS ? seed_subkey(a.seeds[row]) : a.key;
+  if (a.noise == D3S_NOISE_SEEDS) return seed_subkey(a.seeds[row]);
+  if (a.noise == D3S_NOISE_KEYS) return a.keys[(int64_t)row * a.ld_keys];
+  return a.key;
 }
 
 // u for (row, rank r): the word of the [N, k] (one key) or [1, k] (per-row seed)
@@ -309,8 +317,21 @@ __device__ __forceinline__ RawP load_raw(const KArgs &a, int row) {
   r.T = a.T_rows ? a.T_rows[row] : a.T;
   r.p = a.p_rows ? a.p_rows[row] : a.top_p;
   r.tk = a.k_rows ? a.k_rows[row] : a.top_k;
-  r.seed = a.noise == D3S_NOISE_SEEDS ? a.seeds[row] : 0ull;
+  r.seed = 0ull;
+  if (a.noise == D3S_NOISE_SEEDS) {
+    r.seed = a.seeds[row];
+  } else if (a.noise == D3S_NOISE_KEYS) {
+    const uint2 k = a.keys[(int64_t)row * a.ld_keys];
+    r.seed = ((unsigned long long)k.y << 32) | k.x;
+  }
   return r;
+}
+
+// The key that draws the row's uniforms, from its stored parameters.
+__device__ __forceinline__ uint2 raw_key(const KArgs &a, const RawP &r) {
+  if (a.noise == D3S_NOISE_SEEDS) return seed_subkey(r.seed);
+  if (a.noise == D3S_NOISE_KEYS) return make_uint2((unsigned)r.seed, (unsigned)(r.seed >> 32));
+  return a.key;
 }
 
 __device__ __forceinline__ int resolve(const KArgs &a, const RawP &r, RowP &rp) {
@@ -349,7 +370,7 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
 template <int ESZ>
 __device__ __forceinline__ void issue_row(const KArgs &a, int row, unsigned char *stage,
                                           uint64_t *bar, uint64_t pol) {
-  const uintptr_t start = (uintptr_t)a.logits + (uintptr_t)row * (uintptr_t)a.ld * ESZ;
+  const uintptr_t start = (uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ;
   const uintptr_t lo = start & ~(uintptr_t)15;
   const uintptr_t hi = (start + (uintptr_t)a.V * ESZ + 15) & ~(uintptr_t)15;
   const uint32_t bytes = (uint32_t)(hi - lo);
@@ -425,7 +446,7 @@ __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &
   }
   float2 s2 = make_float2(0.0f, 0.0f);
   unsigned long long bits = 0ull;
-  // every term's d >= the row's smallest d: when that is >= -87 the floor is a no-op
+  // every term's d >= the row's smallest d: when that is >= -86 the floor is a no-op
   if (__fsub_rn(__fdiv_rn(xmin, T), gmax) >= kTermFloor)
     sum_and_mask<JJ, false, EXACT>(q, gmax, tau, t, V, s2, bits);
   else
@@ -517,7 +538,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
     const bool ok = mbar_wait_bounded(&sm.mbar[s], (uint32_t)(it / stages) & 1u);
     const unsigned char *rb =
         dsm + (size_t)s * span +
-        (((uintptr_t)a.logits + (uintptr_t)row * (uintptr_t)a.ld * ESZ) & 15);
+        (((uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ) & 15);
     float q[PP][JJ];
     float pm[PP];
     float pmn = f_inf();
@@ -562,6 +583,15 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
     if (__syncthreads_or(!ok)) {
       failed = true;
       break;
+    }
+    if (a.finite && t == 0) {  // every logit finite: no NaN, and the max and min are finite
+      float fx = sm.red_max[par][0], fn = sm.red_min[par][0];
+#pragma unroll
+      for (int i = 1; i < kFastW; ++i) {
+        fx = max_nan(fx, sm.red_max[par][i]);
+        fn = fminf(fn, sm.red_min[par][i]);
+      }
+      a.finite[row] = (fabsf(fx) < f_inf() && fabsf(fn) < f_inf()) ? 1 : 0;
     }
     RowHead &H = heads[row];
     if (pst == D3S_ROW_OK && rp.k <= kFastMaxK) {
@@ -622,6 +652,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
 
 constexpr int kSelWarps = 8;
 constexpr int kSelThreads = 32 * kSelWarps;
+constexpr int kStageCands = 128;  // candidates staged in shared memory per row
 
 __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
   const unsigned lo = __shfl_xor_sync(kFull, (unsigned)v, m);
@@ -654,8 +685,7 @@ __device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int l
           const unsigned long long o = shfl_xor_u64(v[s], stride);
           const bool desc = ((lane + 32 * s) & size) == 0;
           const bool keep_max = ((lane & stride) == 0) == desc;
-          const unsigned long long mx = v[s] > o ? v[s] : o, mn = v[s] > o ? o : v[s];
-          v[s] = keep_max ? mx : mn;
+          v[s] = (v[s] > o) == keep_max ? v[s] : o;
         }
       } else if constexpr (S >= 2) {
         // partners in the same lane: register s and s ^ (stride / 32)
@@ -672,8 +702,9 @@ __device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int l
   }
 }
 
-// Sort the row's C <= 32 S candidates (the first 64 staged in cs, the rest in
-// the slab) with the warp and store the first k keys, in rank order, into sk.
+// Sort the row's C <= 32 S candidates (the first kStageCands staged in cs, the
+// rest in the slab) with the warp and store the first k keys, in rank order,
+// into sk.
 template <int S>
 __device__ __forceinline__ void sort_cands(const unsigned long long *cs, const RowCands &Cs,
                                            int C, int k, unsigned long long *sk, int lane) {
@@ -681,7 +712,7 @@ __device__ __forceinline__ void sort_cands(const unsigned long long *cs, const R
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     const int e = lane + 32 * s;
-    v[s] = e < C ? (e < 64 ? cs[e] : Cs.cand[e]) : 0ull;
+    v[s] = e < C ? (e < kStageCands ? cs[e] : Cs.cand[e]) : 0ull;
   }
   warp_sort_desc<S>(v, lane);
 #pragma unroll
@@ -729,22 +760,29 @@ __device__ __forceinline__ void cp_async_wait_prev() {
   asm volatile("cp.async.wait_group 1;" ::: "memory");
 }
 
-// A row's header and its first 64 candidate slots, staged by cp.async.
+// A row's header and its first candidates, staged by cp.async: as many as the
+// row holds, up to kStageCands (the count is read one row earlier).
 struct alignas(16) SelStage {
   RowHead head;
-  unsigned long long cand[64];
+  unsigned long long cand[kStageCands];
 };
 
 constexpr int kHeadChunks = (int)(sizeof(RowHead) / 16);
 static_assert(sizeof(RowHead) % 16 == 0 && kHeadChunks <= 32, "RowHead is copied in 16-byte chunks");
 
+__device__ __forceinline__ int row_count(const RowHead *heads, int row) {
+  return min(max(heads[row].cnt, 0), kStageCands);
+}
+
 __device__ __forceinline__ void stage_row(const RowHead *heads, const RowCands *cands, int row,
-                                          SelStage &st, int lane) {
+                                          int cnt, SelStage &st, int lane) {
   if (lane < kHeadChunks)
     cp_async16(reinterpret_cast<char *>(&st.head) + 16 * lane,
                reinterpret_cast<const char *>(heads + row) + 16 * lane);
-  cp_async16(reinterpret_cast<char *>(st.cand) + 16 * lane,
-             reinterpret_cast<const char *>(cands + row) + 16 * lane);
+  const int chunks = (cnt + 1) >> 1;  // two keys per 16-byte chunk
+  for (int c = lane; c < chunks; c += 32)
+    cp_async16(reinterpret_cast<char *>(st.cand) + 16 * c,
+               reinterpret_cast<const char *>(cands + row) + 16 * c);
 }
 
 __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KArgs a,
@@ -758,19 +796,24 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
   unsigned long long *sk = sk_all[w];
   int row = gw, b = 0;
   RawP raw;
+  int cnt_next = 0;  // candidate count of row + nw
   if (row < a.N) {
-    stage_row(heads, cands, row, stg_all[w][0], lane);
+    stage_row(heads, cands, row, row_count(heads, row), stg_all[w][0], lane);
     raw = load_raw(a, row);
+    if (row + nw < a.N) cnt_next = row_count(heads, row + nw);
   }
   cp_async_commit();
   for (; row < a.N; row += nw, b ^= 1) {
-    // the next row's header and candidates are copied while this row is sampled
+    // the next row's header and candidates are copied while this row is
+    // sampled, and the count of the row after it is read
     const int nrow = row + nw;
     RawP rawn;
+    int cnt_nn = 0;
     __syncwarp();
     if (nrow < a.N) {
-      stage_row(heads, cands, nrow, stg_all[w][b ^ 1], lane);
+      stage_row(heads, cands, nrow, cnt_next, stg_all[w][b ^ 1], lane);
       rawn = load_raw(a, nrow);
+      if (nrow + nw < a.N) cnt_nn = row_count(heads, nrow + nw);
     }
     cp_async_commit();
     cp_async_wait_prev();
@@ -788,7 +831,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
       } else {
         const RowCands &Cs = cands[row];
         const float lse = __fadd_rn(st.head.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
-        const uint2 key = a.noise == D3S_NOISE_SEEDS ? seed_subkey(raw.seed) : a.key;
+        const uint2 key = raw_key(a, raw);
         if (C <= 32)
           sort_cands<1>(st.cand, Cs, C, rp.k, sk, lane);
         else if (C <= 64)
@@ -802,6 +845,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
       }
     }
     raw = rawn;
+    cnt_next = cnt_nn;
   }
 }
 
@@ -825,6 +869,13 @@ __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a
                : (unsigned)a.N;
   for (unsigned idx = blockIdx.x; idx < nrows; idx += gridDim.x) {
     const int row = use_list ? a.deferred[idx] : (int)idx;
+    if (a.finite && !use_list) {  // (rows handed on by the stats kernel have theirs)
+      const void *b0 = row_base<BF16>(a, row);
+      bool fin = true;
+      for (int i = t; i < V; i += kWideThreads) fin = fin && fabsf(load_x<BF16>(b0, i)) < f_inf();
+      fin = __syncthreads_and(fin);
+      if (t == 0) a.finite[row] = fin ? 1 : 0;
+    }
     RowP rp;
     const int pst = row_params(a, row, rp);
     if (pst != D3S_ROW_OK || rp.k > kcap) {

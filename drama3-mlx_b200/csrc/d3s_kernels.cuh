@@ -30,6 +30,10 @@ struct KArgs {
   float *probs;
   int32_t *topk_ids;
   int64_t ld_out;
+  const uint2 *keys;  // D3S_NOISE_KEYS: row r's key at keys[r * ld_keys]
+  int64_t ld_keys;
+  int32_t *finite;    // optional: 1 when every logit of the row is finite
+  int row_period;     // > 0: row r reads logits row r % row_period (draws sharing logits)
   // scratch (device): rows the fast kernel hands to the wide kernel, the
   // count of those rows, and the wide kernel's completion counter.
   int32_t *deferred;

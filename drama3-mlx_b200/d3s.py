@@ -31,7 +31,7 @@ D3S_ERR_NOMEM = -5
 F32 = 0
 BF16 = 1
 ROW_OK, ROW_NONFINITE, ROW_BADPARAM = 0, 1, 2
-NOISE_KEY, NOISE_SEEDS, NOISE_GIVEN = 0, 1, 2
+NOISE_KEY, NOISE_SEEDS, NOISE_GIVEN, NOISE_KEYS = 0, 1, 2, 3
 MAX_V = 131072
 MAX_K = 16384
 
@@ -67,6 +67,7 @@ class Request(ctypes.Structure):
         ("seeds", ctypes.c_void_p), ("u", ctypes.c_void_p), ("ld_u", ctypes.c_int64),
         ("ids", ctypes.c_void_p), ("status", ctypes.c_void_p), ("kept", ctypes.c_void_p),
         ("probs", ctypes.c_void_p), ("topk_ids", ctypes.c_void_p), ("ld_out", ctypes.c_int64),
+        ("keys", ctypes.c_void_p), ("ld_keys", ctypes.c_int64), ("finite", ctypes.c_void_p),
     ]
 
 
@@ -230,7 +231,10 @@ class Context:
 
     def request(self, logits, ids, *, temperature=1.0, top_p=1.0, top_k=1, temperature_rows=None,
                 top_p_rows=None, top_k_rows=None, noise=NOISE_KEY, key: Key | None = None,
-                seeds=None, u=None, status=None, kept=None, probs=None, topk_ids=None) -> Request:
+                seeds=None, u=None, status=None, kept=None, probs=None, topk_ids=None,
+                keys=None, finite=None) -> Request:
+        """keys: int32/uint32 device tensor [N, 2] (or [N, m, 2]: column 0 of
+        each row is used) for NOISE_KEYS."""
         N, V = logits.shape
         r = Request()
         r.logits = _ptr(logits)
@@ -253,6 +257,9 @@ class Context:
         r.topk_ids = _ptr(topk_ids)
         out = probs if probs is not None else topk_ids
         r.ld_out = out.stride(0) if out is not None else 0
+        r.keys = _ptr(keys)
+        r.ld_keys = (keys.stride(0) // 2) if keys is not None else 0
+        r.finite = _ptr(finite)
         return r
 
     def sample_top_k_top_p(self, logits, temperature: float, top_k: int, top_p: float,
@@ -300,6 +307,23 @@ class Context:
         req = self.request(logits, ids, temperature=T0, top_p=P0, top_k=K0 or 1,
                            temperature_rows=T, top_p_rows=P, top_k_rows=K, noise=NOISE_SEEDS,
                            seeds=seeds, status=status, kept=kept)
+        self.sample(req, stream)
+
+    def sample_rows_keys(self, logits, ids, keys, *, temperature, top_p, top_k, status=None,
+                         finite=None, stream=None) -> None:
+        """Per-row keys (a stream's subkey per row: int32 tensor [N, 2] or
+        [N, m, 2]) and per-row or scalar parameters."""
+        import torch
+
+        def split(x):
+            return (x, 0) if isinstance(x, torch.Tensor) else (None, x)
+
+        T, T0 = split(temperature)
+        P, P0 = split(top_p)
+        K, K0 = split(top_k)
+        req = self.request(logits, ids, temperature=T0, top_p=P0, top_k=K0 or 1,
+                           temperature_rows=T, top_p_rows=P, top_k_rows=K, noise=NOISE_KEYS,
+                           keys=keys, status=status, finite=finite)
         self.sample(req, stream)
 
     def check(self) -> None:

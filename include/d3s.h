@@ -59,6 +59,7 @@ extern "C" {
 #define D3S_NOISE_KEY 0    /* one key for the batch: u = uniform(key, [N, k]) */
 #define D3S_NOISE_SEEDS 1  /* row r draws as d3_sample(row r, seeds[r]) would */
 #define D3S_NOISE_GIVEN 2  /* u given: sample_with_noise */
+#define D3S_NOISE_KEYS 3   /* row r draws u [1, k] from its own subkey keys[r * ld_keys] */
 
 /* limits */
 #define D3S_MAX_V 131072      /* the full-row sum's fixed point holds V <= 2^17 */
@@ -142,6 +143,10 @@ typedef struct {
   float *probs;               /* [N, ld_out] device, optional: race probabilities by rank */
   int32_t *topk_ids;          /* [N, ld_out] device, optional: ids by rank */
   int64_t ld_out;
+  const d3s_key *keys;        /* D3S_NOISE_KEYS: [N * ld_keys] device, 8-byte aligned */
+  int64_t ld_keys;            /* keys between rows (0 means 1) */
+  int32_t *finite;            /* [N] device, optional: 1 when every logit of the row is
+                                 finite (the guard of src/generate.c:92), else 0 */
 } d3s_request;
 
 D3S_API int d3s_sample(d3s_ctx *ctx, const d3s_request *req, void *stream);
@@ -152,7 +157,7 @@ D3S_API int d3s_ctx_check(d3s_ctx *ctx);
 
 /* Test hooks (no counterpart in the reference): y_dev = f(x_dev) with the
  * kernels' own arithmetic; op 0 = exp, 1 = log, 2 = the full-row-sum term
- * exp(max(x, -87)), 3 = x / param by the per-row reciprocal path. */
+ * exp(max(x, -86)), 3 = x / param by the per-row reciprocal path. */
 D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
                            float param, void *stream);
 /* Counts float bit patterns x in [lo, hi) (step `step`) with |x| in

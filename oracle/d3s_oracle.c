@@ -118,11 +118,13 @@ void d3o_uniform(const uint32_t key[2], uint64_t n, float *out) {
 
 /* ------------------------------------------------------------------------ */
 /* exp: Cody & Waite range reduction x = n ln2 + r (n = nearest integer to
- * x log2 e, r by two fused steps against a two-float ln2), exp(r) by its Taylor
- * series to degree 7 in Horner form, then an exact scaling by 2^n (two steps
- * when 2^n is outside the normal range, so subnormal results round once). All
- * constants are the float roundings of log2 e, ln 2 (high part, and the low
- * remainder) and 1/k!. Error below 1.5 ulp over the float range. */
+ * x log2 e, r by two fused steps against a two-float ln2), exp(r) by a
+ * degree-6 polynomial p(r) = 1 + r + r^2 q(r) in Horner form, then an exact
+ * scaling by 2^n (two steps when 2^n is outside the normal range, so subnormal
+ * results round once). Constants: the float roundings of log2 e and ln 2 (high
+ * part and low remainder); q's coefficients minimise the relative error of p on
+ * [-ln2/2, ln2/2] (a linear program over a dense grid, rounded to float).
+ * Error below 1 ulp over the float range. */
 #define D3_L2E 0x1.715476p+0f
 #define D3_LN2_HI 0x1.62e430p-1f
 #define D3_LN2_LO -0x1.05c610p-29f
@@ -134,14 +136,13 @@ float d3o_exp(float x) {
   float t = fmaf(x, D3_L2E, D3_SHIFTER);
   float nf = t - D3_SHIFTER;
   int32_t n = (int32_t)(f2u(t) - f2u(D3_SHIFTER));
-  float r = fmaf(-nf, D3_LN2_HI, x);
-  r = fmaf(-nf, D3_LN2_LO, r);
-  float p = 0x1.a01a02p-13f;          /* 1/7! */
-  p = fmaf(p, r, 0x1.6c16c2p-10f);    /* 1/6! */
-  p = fmaf(p, r, 0x1.111112p-7f);     /* 1/5! */
-  p = fmaf(p, r, 0x1.555556p-5f);     /* 1/4! */
-  p = fmaf(p, r, 0x1.555556p-3f);     /* 1/3! */
-  p = fmaf(p, r, 0.5f);
+  float r = fmaf(nf, -D3_LN2_HI, x);
+  r = fmaf(nf, -D3_LN2_LO, r);
+  float p = 0x1.69d528p-10f;
+  p = fmaf(p, r, 0x1.126946p-7f);
+  p = fmaf(p, r, 0x1.55596cp-5f);
+  p = fmaf(p, r, 0x1.55544p-3f);
+  p = fmaf(p, r, 0x1.fffffcp-2f);
   p = fmaf(p, r, 1.0f);
   p = fmaf(p, r, 1.0f);
   int32_t n2 = n < -126 ? -64 : (n > 127 ? 1 : 0);
@@ -185,13 +186,13 @@ float d3o_log(float x) {
   return fmaf(ef, D3_LN2_HI, fmaf(ef, D3_LN2_LO, L));
 }
 
-/* A term of the full-row sum, d = q - max <= 0: exp(max(d, -87)). Below -87
- * the term (< 2^-125) is far under the 2^-46 resolution of the fixed-point
- * sum; the floor keeps exp's 2^n scale in the normal range. NaN stays NaN (it
- * marks a non-finite row); -inf gives exp(-87). */
+/* A term of the full-row sum, d = q - max <= 0: exp(max(d, -86)). Below -86
+ * the term (< 2^-124) is far under the 2^-46 resolution of the fixed-point
+ * sum; the floor keeps exp's result in the normal range. NaN stays NaN (it
+ * marks a non-finite row); -inf gives exp(-86). */
 static float d3o_exp_term(float d) {
   if (d != d) return d;
-  if (d < -87.0f) d = -87.0f;
+  if (d < -86.0f) d = -86.0f;
   return d3o_exp(d);
 }
 
@@ -535,5 +536,105 @@ void d3o_frame_noise(uint32_t state[2], int n_draws, const int *ks, float *u) {
     d3o_next_key(state, sub);
     d3o_uniform(sub, (uint64_t)ks[d], u);
     u += ks[d];
+  }
+}
+
+int d3o_sample_rows_keys(const void *logits, int dtype, int N, int V, int64_t ld,
+                         const float *temperature, const float *top_p, const int32_t *top_k,
+                         float temperature_all, float top_p_all, int top_k_all,
+                         const uint32_t *keys, int64_t ld_keys, int32_t *ids, int nthreads) {
+  int nbad = 0;
+  if (ld_keys < 1) ld_keys = 1;
+#ifdef _OPENMP
+  if (nthreads < 1) nthreads = omp_get_max_threads();
+#pragma omp parallel num_threads(nthreads) reduction(+ : nbad)
+#endif
+  {
+    float *x = malloc(sizeof(float) * (size_t)V);
+    float *u = malloc(sizeof(float) * (size_t)V);
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 16)
+#endif
+    for (int r = 0; r < N; r++) {
+      float T = temperature ? temperature[r] : temperature_all;
+      float p = top_p ? top_p[r] : top_p_all;
+      int tk = top_k ? top_k[r] : top_k_all;
+      if (tk < 1 || T != T) {
+        ids[r] = -1;
+        nbad++;
+        continue;
+      }
+      int k = tk < V ? tk : V;
+      d3o_uniform(keys + 2 * (size_t)r * (size_t)ld_keys, (uint64_t)k, u);
+      row_to_f32(logits, dtype, ld, r, V, x);
+      ids[r] = d3o_sample_row(x, V, T, p, k, u, NULL, NULL, NULL);
+      if (ids[r] < 0) nbad++;
+    }
+    free(x);
+    free(u);
+  }
+  (void)nthreads;
+  return nbad;
+}
+
+static int32_t candidate_token(int32_t idx, int semantic_start, int eos_id) {
+  return idx == 0 ? eos_id : idx + semantic_start - 1; /* src/tower.c:405-409 */
+}
+
+static int is_semantic(int32_t tok, int semantic_start, int code_vocab) {
+  return tok >= semantic_start && tok <= semantic_start + code_vocab - 1; /* src/tower.c:357-360 */
+}
+
+void d3o_frame_main(const void *logits, int dtype, int V, float temperature, float top_p,
+                    int top_k, const uint32_t key_main[2], const uint32_t key_retry[2],
+                    const int32_t *history, int hist_len, int semantic_start, int code_vocab,
+                    int eos_id, int32_t *main_tok, int32_t *c0, int32_t *flags) {
+  float *x = malloc(sizeof(float) * (size_t)V);
+  float *u = malloc(sizeof(float) * (size_t)V);
+  row_to_f32(logits, dtype, V, 0, V, x);
+  int finite = 1;
+  for (int i = 0; i < V; i++)
+    if (!(x[i] == x[i]) || x[i] == INFINITY || x[i] == -INFINITY) finite = 0;
+  int f = finite ? 0 : D3O_FRAME_NONFINITE;
+  /* noise[0] and noise[1] of the frame (src/tower.c:420-421), k = min(top_k, V) */
+  const int km = top_k < V ? top_k : V;
+  const int kr = D3O_RAS_TOP_K < V ? D3O_RAS_TOP_K : V;
+  int32_t first = -1, retry = -1;
+  if (top_k >= 1 && temperature == temperature) {
+    d3o_uniform(key_main, (uint64_t)km, u);
+    first = d3o_sample_row(x, V, temperature, top_p, km, u, NULL, NULL, NULL);
+  }
+  d3o_uniform(key_retry, (uint64_t)kr, u);
+  retry = d3o_sample_row(x, V, D3O_RAS_TEMPERATURE, D3O_RAS_TOP_P, kr, u, NULL, NULL, NULL);
+  int32_t tok = -1;
+  if (first >= 0 && retry >= 0) {
+    const int32_t t1 = candidate_token(first, semantic_start, eos_id);
+    const int32_t t2 = candidate_token(retry, semantic_start, eos_id);
+    int seen = 0;
+    for (int i = 0; i < hist_len; i++) seen |= history[i] == t1;
+    /* only audio tokens are resampled; a stop is never redrawn (src/tower.c:429-433) */
+    const int repeated = seen && is_semantic(t1, semantic_start, code_vocab);
+    tok = repeated ? t2 : t1;
+    if (repeated) f |= D3O_FRAME_RETRY;
+    if (tok == eos_id) f |= D3O_FRAME_EOS;
+  } else {
+    f |= D3O_FRAME_NONFINITE;
+  }
+  int32_t c = tok - semantic_start;
+  if (tok < 0) c = 0;
+  c = c < 0 ? 0 : (c > code_vocab - 1 ? code_vocab - 1 : c);
+  *main_tok = tok;
+  *c0 = c;
+  *flags = f;
+  free(x);
+  free(u);
+}
+
+void d3o_history_push(int32_t *history, int *hist_len, int32_t tok) {
+  if (*hist_len == D3O_RAS_WINDOW) {
+    for (int i = 1; i < D3O_RAS_WINDOW; i++) history[i - 1] = history[i];
+    history[D3O_RAS_WINDOW - 1] = tok;
+  } else {
+    history[(*hist_len)++] = tok;
   }
 }

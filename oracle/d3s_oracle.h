@@ -26,12 +26,12 @@
  *
  * Floating-point conventions shared with the CUDA kernels (all IEEE binary32,
  * round-to-nearest-even, no contraction: build with -ffp-contract=off):
- *   - exp and log are d3o_exp / d3o_log below (Cody-Waite reduction + Taylor /
- *     atanh series), not libm, so the CPU and GPU agree bit for bit.
+ *   - exp and log are d3o_exp / d3o_log below (Cody-Waite reduction + a
+ *     degree-6 polynomial / atanh series), not libm, so the CPU and GPU agree bit for bit.
  *   - the full-row sum of exp(q - max) is taken as 256 strided partials
  *     (partial p sums elements p, p+256, ... in order, in float), each partial
  *     truncated to a 2^-46 fixed-point uint64 and the partials added exactly.
- *     Each term is exp(max(q - max, -87)): below -87 a term is far under the
+ *     Each term is exp(max(q - max, -86)): below -86 a term is far under the
  *     fixed point's resolution, and the floor keeps exp's scale normal.
  *   - the row maximum ignores the sign of zero (-0 and +0 compare equal, as in
  *     every comparison of the path); top-k order is (value desc, id asc).
@@ -66,7 +66,7 @@ float d3o_exp(float x);
 float d3o_log(float x);
 void d3o_exp_array(const float *x, float *y, int64_t n);
 void d3o_log_array(const float *x, float *y, int64_t n);
-/* the full-row-sum term: exp(max(d, -87)) */
+/* the full-row-sum term: exp(max(d, -86)) */
 void d3o_term_array(const float *x, float *y, int64_t n);
 
 /* ---- sampler ---- */
@@ -120,6 +120,41 @@ int d3o_sample_rows(const void *logits, int dtype, int N, int V, int64_t ld,
  * uniform draws from the global state, in order. ks[i] = k of draw i.
  * Writes the concatenated uniforms into u (sum of ks floats). */
 void d3o_frame_noise(uint32_t state[2], int n_draws, const int *ks, float *u);
+
+/* Per-row keys: row r draws u [1, k] from keys[2 * r * ld_keys ..] (a
+ * stream's own subkey, as sample_noise(1, V, top_k) on that stream's key
+ * sequence would). Null parameter arrays fall back to the scalars. Returns the
+ * number of flagged rows (ids -1). */
+int d3o_sample_rows_keys(const void *logits, int dtype, int N, int V, int64_t ld,
+                         const float *temperature, const float *top_p, const int32_t *top_k,
+                         float temperature_all, float top_p_all, int top_k_all,
+                         const uint32_t *keys, int64_t ld_keys, int32_t *ids, int nthreads);
+
+/* The sampling part of tower_decode_step (src/tower.c:405-433) for one
+ * stream: the main draw (user T / top_p / top_k, key_main), the retry draw
+ * (RAS: T 1.0, top_p 0.95, top_k 30, key_retry, src/tower.c:14-16), both on the
+ * same backbone logits row; candidate_token maps index 0 to eos_id and i >= 1
+ * to semantic_start + i - 1; a semantic first token found among the
+ * hist_len history tokens is replaced by the retry token. Writes the frame's
+ * main token, c0 = clip(main - semantic_start, 0, code_vocab - 1) and flags
+ * (D3O_FRAME_*). A row with non-finite logits (the reference's die() at
+ * src/generate.c:92) gets main -1, c0 0 and the NONFINITE flag. */
+#define D3O_RAS_TEMPERATURE 1.0f
+#define D3O_RAS_TOP_P 0.95f
+#define D3O_RAS_TOP_K 30
+#define D3O_RAS_WINDOW 16
+#define D3O_FRAME_EOS 1
+#define D3O_FRAME_NONFINITE 2
+#define D3O_FRAME_RETRY 4
+void d3o_frame_main(const void *logits, int dtype, int V, float temperature, float top_p,
+                    int top_k, const uint32_t key_main[2], const uint32_t key_retry[2],
+                    const int32_t *history, int hist_len, int semantic_start, int code_vocab,
+                    int eos_id, int32_t *main_tok, int32_t *c0, int32_t *flags);
+
+/* The history step of the decode loop (src/generate.c:97-100): append tok to
+ * the window of the last D3O_RAS_WINDOW main tokens, dropping the oldest when
+ * full. */
+void d3o_history_push(int32_t *history, int *hist_len, int32_t tok);
 
 #ifdef __cplusplus
 }

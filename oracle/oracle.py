@@ -118,6 +118,16 @@ def lib():
                                       ctypes.c_float, ctypes.c_int, ctypes.c_uint64, _i32p,
                                       ctypes.c_int]
         L.d3o_frame_noise.argtypes = [_u32p, ctypes.c_int, _i32p, _f32p]
+        L.d3o_sample_rows_keys.restype = ctypes.c_int
+        L.d3o_sample_rows_keys.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int64, _f32p, _f32p, _i32p, ctypes.c_float,
+                                           ctypes.c_float, ctypes.c_int, _u32p, ctypes.c_int64,
+                                           _i32p, ctypes.c_int]
+        L.d3o_frame_main.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_int, _u32p, _u32p, _i32p,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     _i32p, _i32p, _i32p]
+        L.d3o_history_push.argtypes = [_i32p, ctypes.POINTER(ctypes.c_int), ctypes.c_int32]
         _lib = L
     return _lib
 
@@ -195,7 +205,7 @@ def log(x: np.ndarray) -> np.ndarray:
 
 
 def exp_term(x: np.ndarray) -> np.ndarray:
-    """The full-row-sum term exp(max(d, -87))."""
+    """The full-row-sum term exp(max(d, -86))."""
     x = np.ascontiguousarray(x, np.float32)
     y = np.empty_like(x)
     lib().d3o_term_array(_p(x, _f32p), _p(y, _f32p), x.size)
@@ -300,3 +310,65 @@ def frame_noise(state: np.ndarray, ks) -> np.ndarray:
     u = np.zeros(int(ks.sum()), np.float32)
     lib().d3o_frame_noise(_p(state, _u32p), len(ks), _p(ks, _i32p), _p(u, _f32p))
     return u
+
+
+def sample_rows_keys(logits: np.ndarray, temperature, top_p, top_k, keys: np.ndarray,
+                     nthreads: int = 0) -> np.ndarray:
+    """Per-row keys: keys uint32 [N, 2] (or [N, m, 2]: column 0 of each row is
+    used, as a key array with ld_keys = m). Parameters are arrays or scalars."""
+    lg, dt = _logits(logits)
+    N, V = lg.shape
+    keys = np.ascontiguousarray(keys, np.uint32)
+    ld_keys = 1 if keys.ndim == 2 else keys.shape[1]
+
+    def arr(x, dtype):
+        if np.isscalar(x):
+            return None, x
+        return np.ascontiguousarray(np.asarray(x, dtype)[:N]), 0
+
+    T, T0 = arr(temperature, np.float32)
+    P, P0 = arr(top_p, np.float32)
+    K, K0 = arr(top_k, np.int32)
+    ids = np.zeros(N, np.int32)
+    lib().d3o_sample_rows_keys(lg.ctypes.data, dt, N, V, V, _p(T, _f32p), _p(P, _f32p),
+                               _p(K, _i32p), float(T0), float(P0), int(K0), _p(keys, _u32p),
+                               ld_keys, _p(ids, _i32p), nthreads)
+    return ids
+
+
+RAS_WINDOW = 16
+FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
+
+
+def frame_main(logits_row: np.ndarray, temperature: float, top_p: float, top_k: int, key_main,
+               key_retry, history, semantic_start: int, code_vocab: int, eos_id: int):
+    """tower_decode_step's sampling of one stream: (main_tok, c0, flags)."""
+    lg, dt = _logits(np.asarray(logits_row).reshape(1, -1))
+    V = lg.shape[1]
+    h = np.ascontiguousarray(np.asarray(history, np.int32).reshape(-1))
+    out = np.zeros(3, np.int32)
+    lib().d3o_frame_main(lg.ctypes.data, dt, V, temperature, top_p, top_k, _p(_key(key_main), _u32p),
+                         _p(_key(key_retry), _u32p), _p(h, _i32p), len(h), semantic_start,
+                         code_vocab, eos_id, _p(out[0:1], _i32p), _p(out[1:2], _i32p),
+                         _p(out[2:3], _i32p))
+    return int(out[0]), int(out[1]), int(out[2])
+
+
+def history_push(history: list, tok: int) -> list:
+    """The decode loop's history window step (drop the oldest when full)."""
+    h = list(history) + [int(tok)]
+    return h[-RAS_WINDOW:]
+
+
+def streams_next_keys(states: np.ndarray, n: int):
+    """Advance each stream's key n times: (new states [S, 2], subkeys [S, n, 2])."""
+    states = np.array(states, np.uint32).reshape(-1, 2)
+    subs = np.zeros((states.shape[0], n, 2), np.uint32)
+    for s in range(states.shape[0]):
+        st = np.ascontiguousarray(states[s])
+        for i in range(n):
+            sub = np.zeros(2, np.uint32)
+            lib().d3o_next_key(_p(st, _u32p), _p(sub, _u32p))
+            subs[s, i] = sub
+        states[s] = st
+    return states, subs

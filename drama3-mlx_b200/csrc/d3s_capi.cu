@@ -23,6 +23,7 @@ struct d3s_ctx {
   size_t logits_cap = 0;  // floats
   size_t rows_cap = 0;
   cudaStream_t stream = nullptr;
+  d3s::FrameScratch frame;  // d3s_frame_main's per-draw arrays
 };
 
 namespace {
@@ -209,6 +210,34 @@ int take_subkey(d3s_key *state, d3s_key *sub) {
 
 int d3s::set_error(int code, const char *msg) { return fail(code, "%s", msg); }
 
+namespace {
+
+// One allocation holds the 2S-entry arrays of d3s_frame_main.
+int reserve_frame(d3s_ctx *ctx, int64_t streams) {
+  d3s::FrameScratch &f = ctx->frame;
+  if (f.capacity >= streams) return D3S_OK;
+  const int64_t cap = std::max<int64_t>(streams, 256), n = 2 * cap;
+  const size_t bytes = (size_t)n * (sizeof(uint2) + 2 * sizeof(float) + 3 * sizeof(int32_t));
+  unsigned char *base = nullptr;
+  const cudaError_t e = cudaMalloc(&base, bytes);
+  if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "frame scratch: %s", cudaGetErrorString(e));
+  if (f.keys) {
+    cudaDeviceSynchronize();  // queued frames may still use the old arrays
+    cudaFree(f.keys);         // the allocation's base
+  }
+  // keys first: the one 8-byte type keeps its alignment
+  f.keys = reinterpret_cast<uint2 *>(base);
+  f.T = reinterpret_cast<float *>(f.keys + n);
+  f.p = f.T + n;
+  f.k = reinterpret_cast<int32_t *>(f.p + n);
+  f.ids = f.k + n;
+  f.finite = f.ids + n;
+  f.capacity = cap;
+  return D3S_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int d3s_version(void) { return D3S_VERSION; }
@@ -289,6 +318,7 @@ void d3s_ctx_destroy(d3s_ctx *ctx) {
   cudaFree(ctx->h_logits_dev);
   cudaFree(ctx->ids_dev);
   cudaFree(ctx->status_dev);
+  cudaFree(ctx->frame.keys);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -401,6 +431,74 @@ int d3s_ctx_check(d3s_ctx *ctx) {
     cudaMemset(ctx->scratch.counters + 2, 0, sizeof(uint32_t));
     return fail(D3S_ERR_CUDA, "a sampler kernel gave up waiting for a row copy (rows left unsampled)");
   }
+  return D3S_OK;
+}
+
+// ---- one decode frame ----
+
+int d3s_keys_next(d3s_ctx *ctx, d3s_key *state_dev, int S, int n, d3s_key *sub_dev,
+                  int64_t ld_sub, void *stream) {
+  if (!ctx) return fail(D3S_ERR_ARG, "null ctx");
+  if (S < 0 || n < 0) return fail(D3S_ERR_ARG, "bad S=%d / n=%d", S, n);
+  if (S > 0 && n > 0 && (!state_dev || !sub_dev)) return fail(D3S_ERR_ARG, "null state or sub");
+  if (ld_sub < n) return fail(D3S_ERR_ARG, "ld_sub=%lld < n=%d", (long long)ld_sub, n);
+  if ((((uintptr_t)state_dev | (uintptr_t)sub_dev) & 7) != 0)
+    return fail(D3S_ERR_ARG, "key arrays must be 8-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  const int rc = d3s::launch_keys_next(reinterpret_cast<uint2 *>(state_dev), S, n,
+                                       reinterpret_cast<uint2 *>(sub_dev), ld_sub,
+                                       (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "key launch");
+  return D3S_OK;
+}
+
+int d3s_frame_main(d3s_ctx *ctx, const d3s_frame_request *f, void *stream) {
+  if (!ctx || !f) return fail(D3S_ERR_ARG, "null ctx or request");
+  if (f->S < 0 || f->V < 1) return fail(D3S_ERR_ARG, "bad shape S=%d V=%d", f->S, f->V);
+  if (f->V > D3S_MAX_V) return fail(D3S_ERR_UNSUPPORTED, "V=%d exceeds %d", f->V, D3S_MAX_V);
+  if (f->dtype != D3S_F32 && f->dtype != D3S_BF16) return fail(D3S_ERR_ARG, "bad dtype %d", f->dtype);
+  if (f->ld < f->V) return fail(D3S_ERR_ARG, "ld < V");
+  if (f->top_k < 1) return fail(D3S_ERR_ARG, "top_k=%d < 1", f->top_k);
+  if (std::min(f->top_k, f->V) > D3S_MAX_K)
+    return fail(D3S_ERR_UNSUPPORTED, "k=%d exceeds %d", std::min(f->top_k, f->V), D3S_MAX_K);
+  if (f->temperature != f->temperature) return fail(D3S_ERR_ARG, "temperature is NaN");
+  if (f->code_vocab < 1) return fail(D3S_ERR_ARG, "code_vocab=%d < 1", f->code_vocab);
+  if (f->ld_keys < 2) return fail(D3S_ERR_ARG, "ld_keys=%lld < 2", (long long)f->ld_keys);
+  if (f->S > 0 && (!f->logits || !f->keys || !f->history || !f->hist_len || !f->main_tok || !f->c0))
+    return fail(D3S_ERR_ARG, "null logits / keys / history / hist_len / main_tok / c0");
+  if (((uintptr_t)f->keys & 7) != 0) return fail(D3S_ERR_ARG, "keys must be 8-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  int rc = reserve_scratch(ctx, 2 * (int64_t)f->S);
+  if (rc == D3S_OK) rc = reserve_frame(ctx, f->S);
+  if (rc != D3S_OK) return rc;
+  d3s_request r{};
+  r.logits = f->logits;
+  r.dtype = f->dtype;
+  r.N = 2 * f->S;
+  r.V = f->V;
+  r.ld = f->ld;
+  r.noise = D3S_NOISE_KEYS;
+  const d3s::KArgs a = to_kargs(&r, ctx);
+  d3s::FrameArgs fa;
+  fa.S = f->S;
+  fa.temperature = f->temperature;
+  fa.top_p = f->top_p;
+  fa.top_k = f->top_k;
+  fa.keys = reinterpret_cast<const uint2 *>(f->keys);
+  fa.ld_keys = f->ld_keys;
+  fa.history = f->history;
+  fa.hist_len = f->hist_len;
+  fa.semantic_start = f->semantic_start;
+  fa.code_vocab = f->code_vocab;
+  fa.eos_id = f->eos_id;
+  fa.update_history = f->update_history;
+  fa.main_tok = f->main_tok;
+  fa.c0 = f->c0;
+  fa.flags = f->flags;
+  rc = d3s::launch_frame(fa, ctx->frame, a, ctx->scratch, (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "frame launch");
   return D3S_OK;
 }
 

@@ -74,6 +74,31 @@ struct Scratch {
 // Launch the sampler for one request. Validates sizes; returns D3S_* status.
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t stream);
 
+// One decode frame's main + retry draws for S streams (d3s_frame_request).
+struct FrameArgs {
+  int S;
+  float temperature, top_p;
+  int top_k;
+  const uint2 *keys;
+  int64_t ld_keys;
+  int32_t *history;
+  int32_t *hist_len;
+  int semantic_start, code_vocab, eos_id, update_history;
+  int32_t *main_tok, *c0, *flags;
+};
+// Device arrays of 2S entries (rows [0, S) main, [S, 2S) retry).
+struct FrameScratch {
+  float *T = nullptr, *p = nullptr;
+  int32_t *k = nullptr, *ids = nullptr, *finite = nullptr;
+  uint2 *keys = nullptr;
+  int64_t capacity = 0;  // streams
+};
+// `a` carries the logits (logits, dtype, V, ld) and the scratch pointers.
+int launch_frame(const FrameArgs &f, const FrameScratch &fs, KArgs a, const Scratch &sc,
+                 cudaStream_t stream);
+// Advance S key states by n splits each; subkeys at sub[s * ld_sub + i].
+int launch_keys_next(uint2 *state, int S, int n, uint2 *sub, int64_t ld_sub, cudaStream_t stream);
+
 // Record an error message for d3s_last_error() on this thread; returns code.
 int set_error(int code, const char *msg);
 

@@ -40,7 +40,9 @@ EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split"
            "d3s_next_key", "d3s_ctx_create", "d3s_ctx_destroy", "d3s_ctx_reserve",
            "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
            "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3s_sample_rows_static",
-           "d3_sample", "d3s_last_status")
+           "d3_sample", "d3s_last_status", "d3s_keys_next", "d3s_frame_main")
+RAS_WINDOW = 16
+FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
 STATIC_MAX_ROWS = 4096
 
 
@@ -68,6 +70,18 @@ class Request(ctypes.Structure):
         ("ids", ctypes.c_void_p), ("status", ctypes.c_void_p), ("kept", ctypes.c_void_p),
         ("probs", ctypes.c_void_p), ("topk_ids", ctypes.c_void_p), ("ld_out", ctypes.c_int64),
         ("keys", ctypes.c_void_p), ("ld_keys", ctypes.c_int64), ("finite", ctypes.c_void_p),
+    ]
+
+
+class FrameRequest(ctypes.Structure):
+    _fields_ = [
+        ("logits", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("S", ctypes.c_int32),
+        ("V", ctypes.c_int32), ("ld", ctypes.c_int64), ("temperature", ctypes.c_float),
+        ("top_p", ctypes.c_float), ("top_k", ctypes.c_int32), ("keys", ctypes.c_void_p),
+        ("ld_keys", ctypes.c_int64), ("history", ctypes.c_void_p), ("hist_len", ctypes.c_void_p),
+        ("semantic_start", ctypes.c_int32), ("code_vocab", ctypes.c_int32),
+        ("eos_id", ctypes.c_int32), ("update_history", ctypes.c_int32),
+        ("main_tok", ctypes.c_void_p), ("c0", ctypes.c_void_p), ("flags", ctypes.c_void_p),
     ]
 
 
@@ -117,6 +131,8 @@ def lib() -> ctypes.CDLL:
                                 ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_int32)]
         L.d3_sample.restype = None
         L.d3s_last_status.restype = i32
+        L.d3s_keys_next.argtypes = [vp, vp, i32, i32, vp, i64, vp]
+        L.d3s_frame_main.argtypes = [vp, ctypes.POINTER(FrameRequest), vp]
         _lib = L
     return _lib
 
@@ -325,6 +341,44 @@ class Context:
                            temperature_rows=T, top_p_rows=P, top_k_rows=K, noise=NOISE_KEYS,
                            keys=keys, status=status, finite=finite)
         self.sample(req, stream)
+
+    def keys_next(self, states, n: int, sub=None, stream=None):
+        """Advance each stream's key (int32 device tensor [S, 2], in place) n
+        times; returns the subkeys [S, n, 2] in draw order."""
+        import torch
+        S = states.shape[0]
+        if sub is None:
+            sub = torch.empty(S, n, 2, dtype=torch.int32, device=states.device)
+        _check(lib().d3s_keys_next(self._h, _ptr(states), S, n, _ptr(sub), sub.stride(0) // 2,
+                                   _stream_ptr(stream)))
+        return sub
+
+    def frame_main(self, logits, sub, history, hist_len, *, temperature: float, top_p: float,
+                   top_k: int, semantic_start: int, code_vocab: int, eos_id: int,
+                   update_history: bool = True, stream=None):
+        """tower_decode_step's main + retry draws for S streams: logits [S, V]
+        device, sub [S, n, 2] (the frame's subkeys: 0 main, 1 retry), history
+        int32 [S, RAS_WINDOW], hist_len int32 [S]. Returns (main_tok, c0, flags)."""
+        import torch
+        S, V = logits.shape
+        dev = logits.device
+        main_tok = torch.empty(S, dtype=torch.int32, device=dev)
+        c0 = torch.empty(S, dtype=torch.int32, device=dev)
+        flags = torch.empty(S, dtype=torch.int32, device=dev)
+        f = FrameRequest()
+        f.logits = _ptr(logits)
+        f.dtype = _dtype_code(logits)
+        f.S, f.V, f.ld = S, V, logits.stride(0)
+        f.temperature, f.top_p, f.top_k = float(temperature), float(top_p), int(top_k)
+        f.keys = _ptr(sub)
+        f.ld_keys = sub.stride(0) // 2
+        f.history = _ptr(history)
+        f.hist_len = _ptr(hist_len)
+        f.semantic_start, f.code_vocab, f.eos_id = semantic_start, code_vocab, eos_id
+        f.update_history = 1 if update_history else 0
+        f.main_tok, f.c0, f.flags = _ptr(main_tok), _ptr(c0), _ptr(flags)
+        _check(lib().d3s_frame_main(self._h, ctypes.byref(f), _stream_ptr(stream)))
+        return main_tok, c0, flags
 
     def check(self) -> None:
         """Synchronise and raise if a kernel recorded a failure (a bounded wait)."""

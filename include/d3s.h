@@ -190,6 +190,47 @@ D3S_API int d3s_sample_rows_static(const void *logits_dev, int dtype, int N, int
                                    const int32_t *top_k_dev, const uint64_t *seeds_dev,
                                    int32_t *ids_dev, void *stream);
 
+/* ---- one decode frame: tower_decode_step's draws (src/tower.c:405-452) ---- */
+
+/* Advance S streams' key states (device [S], 8-byte aligned) by n splits each,
+ * as n calls of the key sequence's next(), writing the subkeys in draw order
+ * to sub_dev[s * ld_sub + i]. A frame of tower_decode_step takes
+ * n = 2 + (n_codebooks - 1): main, retry, then one per codebook head
+ * (src/tower.c:417-424). */
+D3S_API int d3s_keys_next(d3s_ctx *ctx, d3s_key *state_dev, int S, int n, d3s_key *sub_dev,
+                          int64_t ld_sub, void *stream);
+
+#define D3S_RAS_WINDOW 16      /* main tokens a frame is checked against (src/generate.h:11) */
+#define D3S_FRAME_EOS 1        /* flags: the frame's main token is eos_id */
+#define D3S_FRAME_NONFINITE 2  /* the logits row holds NaN or +-inf (src/generate.c:92) */
+#define D3S_FRAME_RETRY 4      /* the RAS retry token replaced a repeated semantic token */
+
+typedef struct {
+  const void *logits;          /* [S, ld] device: backbone audio logits, index 0 = eos,
+                                  i >= 1 = semantic_start + i - 1 */
+  int32_t dtype, S, V;
+  int64_t ld;
+  float temperature, top_p;    /* SamplingParams (src/model.h:146-150) of the main draw */
+  int32_t top_k;
+  const d3s_key *keys;         /* device, 8-byte aligned: stream s's frame subkeys at
+                                  keys[s * ld_keys + i], i = 0 main, 1 retry */
+  int64_t ld_keys;
+  int32_t *history;            /* [S, D3S_RAS_WINDOW] device: last main tokens, oldest first */
+  int32_t *hist_len;           /* [S] device: valid history entries per stream */
+  int32_t semantic_start, code_vocab, eos_id;  /* model config (src/model.h:27-29) */
+  int32_t update_history;      /* 1: append each main token to its window (src/generate.c:97-100) */
+  int32_t *main_tok;           /* [S] device: codes[0], -1 when a draw was flagged */
+  int32_t *c0;                 /* [S] device: codes[1] = clip(main - semantic_start, 0, code_vocab - 1) */
+  int32_t *flags;              /* [S] device, optional: D3S_FRAME_* bits */
+} d3s_frame_request;
+
+/* The main and the retry draw of S streams from one pass of kernels (rows s
+ * and S + s of one batch read logits row s), then candidate_token, the
+ * repetition check, c0 and the flags (src/tower.c:425-437). The codebook
+ * heads of the frame are plain d3s_sample calls with D3S_NOISE_KEYS and
+ * keys = sub + 2 + j, ld_keys = n. */
+D3S_API int d3s_frame_main(d3s_ctx *ctx, const d3s_frame_request *req, void *stream);
+
 /* ---- the reference's test C-ABI (src/testapi.c:155-166) ---- */
 
 /* Host logits [N, V] f32 -> host ids [N]: seeds the global key with `seed`,

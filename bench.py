@@ -52,6 +52,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--workload", choices=["c5", "c3", "c4"], default="c5",
+                    help="c5: the headline line; c3 (lm_head + sample) and c4 (tower frames) "
+                         "print their own lines for the design notes")
+    ap.add_argument("--batch", type=int, default=1024, help="c3: hidden-state rows B")
+    ap.add_argument("--frames", type=int, default=200, help="c4: frames per stream")
     return ap.parse_args()
 
 
@@ -359,12 +364,13 @@ def run_ours(args):
                        "l2": "inputs 1.07 GB per GPU > 126 MB L2 (no flush needed)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "sample_fast_kernel<17,f32> + sample_wide_kernel (empty hand-off)",
+                         "kernel": "one sampler call: sample_stats_kernel<17,f32> + "
+                                   "sample_select_kernel + sample_wide_kernel (empty hand-off)",
                          "kernel_ms": kernel_ms, "kernel_ms_max_over_ranks": kernel_ms_max,
                          "bytes_per_launch": bytes_per_launch},
             "clocks": clocks,
             "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "cpu_baseline": cpu,
             "latency": latency,
         }
@@ -375,10 +381,165 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def _events_ms(torch, fn, steps: int, warmup: int = 3) -> float:
+    """Mean device time of fn() over `steps` calls (CUDA events, current stream)."""
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(steps):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def load_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        for key in ("bf16_tflops", "bf16_tflops_burst"):
+            if key in d:
+                return float(d[key]), "measured"
+    return 1590.0, "fallback"
+
+
+def run_c3(args):
+    """Config 3: the lm_head projection (h [B, 2048] x W [4097, 2048]^T, bf16
+    logits) and the fused projection + sample call, one GPU."""
+    import torch
+
+    import d3s
+    import synth
+    torch.cuda.set_device(0)
+    B, D = args.batch, 2048
+    ctx = d3s.Context(0)
+    ctx.reserve(max(B, 1024))
+    h, W = synth.c3_inputs(B, seed=7)
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device="cuda")
+    ids = torch.empty(B, dtype=torch.int32, device="cuda")
+    seeds = torch.arange(B, dtype=torch.int64, device="cuda")
+    # the weight (16.8 MB) fits in L2: flush between projection launches so each one
+    # reads W from HBM, as a decode step that ran the backbone in between would
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def proj():
+        ctx.lmhead(h, W, out=logits)
+
+    def fused():
+        ctx.lmhead_sample(h, W, logits, ids, temperature=0.7, top_p=0.7, top_k=30,
+                          noise=d3s.NOISE_SEEDS, seeds=seeds)
+
+    evs = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        proj()
+        b.record(st)
+        if i >= args.warmup:
+            evs.append((a, b))
+    torch.cuda.synchronize()
+    proj_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    evs = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fused()
+        b.record(st)
+        if i >= args.warmup:
+            evs.append((a, b))
+    torch.cuda.synchronize()
+    ctx.check()
+    fused_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    peak_gbs, gkind = load_peaks()
+    peak_tf, tkind = load_tflops()
+    bytes_ = V * D * 2 + B * D * 2 + B * V * 2
+    flops = 2.0 * B * V * D
+    gbs = bytes_ / (proj_ms / 1e3) / 1e9
+    tfs = flops / (proj_ms / 1e3) / 1e12
+    tensor = B > 64
+    line = {
+        "metric": "lm_head + sample rows/s (config 3)", "value": B / (fused_ms / 1e3), "unit": "rows/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fused_ms,
+        "higher_is_better": True, "dtype": "bf16 x bf16 -> f32 accumulate -> bf16 logits",
+        "data": "synthetic", "config": {"workload": f"config3: h bf16 [{B}, {D}] ~N(0,1), W bf16 [{V}, {D}] "
+                                        "~N(0,0.02), T 0.7, top_p 0.7, top_k 30, per-row seeds",
+                                        "l2": "256 MB buffer written between launches"},
+        "projection_ms": proj_ms,
+        "projection_kernel": "lmhead_gemv_kernel" if B <= 8 else "lmhead_gemm_kernel (tcgen05)",
+        "roofline": ({"bound": "tensor", "achieved": tfs, "peak": peak_tf, "unit": "TFLOP/s",
+                      "frac": tfs / peak_tf, "peak_source": tkind} if tensor else
+                     {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s",
+                      "frac": gbs / peak_gbs, "peak_source": gkind}),
+        "hbm_gbs": gbs, "tflops": tfs,
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def run_c4(args):
+    """Config 4: 512 streams x 9 codebook heads per frame (bf16 [512, 1024] rows,
+    Zipf-biased), T 1.0, top_p 0.9, top_k 30, per-stream keys advanced in
+    tower_decode_step order; plus each frame's main + retry draw on a [512, 4097]
+    backbone row. One GPU, all frames' logits generated up front per frame set."""
+    import torch
+
+    import d3s
+    import synth
+    torch.cuda.set_device(0)
+    S, H, Vh = 512, 9, 1024
+    ctx = d3s.Context(0)
+    ctx.reserve(2 * S)
+    bias = synth.zipf_bias(Vh, 11)
+    heads = [synth.c4_logits(S, seed=100 + j, V=Vh, bias=bias) for j in range(H)]
+    xb = synth.c1_rows(S, seed=5).to(torch.bfloat16)
+    states = torch.randint(0, 2**31 - 1, (S, 2), dtype=torch.int32, device="cuda")
+    hist = torch.zeros(S, 16, dtype=torch.int32, device="cuda")
+    hl = torch.zeros(S, dtype=torch.int32, device="cuda")
+    sub = torch.empty(S, 2 + H, 2, dtype=torch.int32, device="cuda")
+    ids = torch.empty(S, dtype=torch.int32, device="cuda")
+
+    def frame():
+        ctx.keys_next(states, 2 + H, sub=sub)
+        ctx.frame_main(xb, sub, hist, hl, temperature=1.0, top_p=0.9, top_k=30,
+                       semantic_start=1000, code_vocab=4096, eos_id=7)
+        for j in range(H):
+            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9, top_k=30)
+
+    def heads_only():
+        for j in range(H):
+            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9, top_k=30)
+
+    frames = max(1, args.frames)
+    frame_ms = _events_ms(torch, frame, frames)
+    heads_ms = _events_ms(torch, heads_only, frames)
+    ctx.check()
+    line = {
+        "metric": "tower head rows/s (config 4)", "value": S * H / (heads_ms / 1e3), "unit": "rows/s",
+        "n_gpus": 1, "frames": frames, "ms_per_frame_heads": heads_ms, "ms_per_frame_all": frame_ms,
+        "frame_rows_per_s": S * (H + 2) / (frame_ms / 1e3), "higher_is_better": True,
+        "dtype": "bf16 logits, f32 math", "data": "synthetic",
+        "config": {"workload": "config4: 512 streams x 9 heads, V=1024 bf16 ~N(0,2.5)+Zipf(1.1); "
+                               "frame main+retry on [512, 4097] bf16; T 1.0, top_p 0.9, top_k 30"},
+        "note": "a head launch is 512 rows: launch-bound; rows stay in L2",
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c3":
+        run_c3(args)
+    elif args.workload == "c4":
+        run_c4(args)
     else:
         run_ours(args)
 

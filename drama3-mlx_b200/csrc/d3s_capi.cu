@@ -502,6 +502,53 @@ int d3s_frame_main(d3s_ctx *ctx, const d3s_frame_request *f, void *stream) {
   return D3S_OK;
 }
 
+// ---- the lm_head projection ----
+
+static int check_lmhead(const void *h, int64_t ld_h, const void *W, int64_t ld_w, int B, int V,
+                        int D, const void *out, int64_t ld_out) {
+  if (B < 0 || V < 1 || D < 8) return fail(D3S_ERR_ARG, "bad shape B=%d V=%d D=%d", B, V, D);
+  if (V > D3S_MAX_V) return fail(D3S_ERR_UNSUPPORTED, "V=%d exceeds %d", V, D3S_MAX_V);
+  if (B > 0 && (!h || !W || !out)) return fail(D3S_ERR_ARG, "null h / W / logits");
+  if (D % 8 || ld_h < D || ld_w < D || ld_h % 8 || ld_w % 8 || ld_out < V)
+    return fail(D3S_ERR_ARG, "D, ld_h, ld_w must be multiples of 8 (16-byte rows), ld >= D, ld_logits >= V");
+  if ((((uintptr_t)h | (uintptr_t)W) & 15) != 0) return fail(D3S_ERR_ARG, "h and W must be 16-byte aligned");
+  if (((uintptr_t)out & 1) != 0) return fail(D3S_ERR_ARG, "logits must be 2-byte aligned");
+  return D3S_OK;
+}
+
+int d3s_lmhead(d3s_ctx *ctx, const void *h_dev, int64_t ld_h, const void *W_dev, int64_t ld_w,
+               int B, int V, int D, void *logits_dev, int64_t ld_logits, void *stream) {
+  if (!ctx) return fail(D3S_ERR_ARG, "null ctx");
+  int rc = check_lmhead(h_dev, ld_h, W_dev, ld_w, B, V, D, logits_dev, ld_logits);
+  if (rc != D3S_OK) return rc;
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  d3s::LmArgs a;
+  a.h = h_dev;
+  a.ld_h = ld_h;
+  a.W = W_dev;
+  a.ld_w = ld_w;
+  a.B = B;
+  a.V = V;
+  a.D = D;
+  a.out = logits_dev;
+  a.ld_out = ld_logits;
+  a.error = reinterpret_cast<int32_t *>(ctx->scratch.counters + 2);
+  rc = d3s::launch_lmhead(a, (cudaStream_t)stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "lm_head launch");
+  return D3S_OK;
+}
+
+int d3s_lmhead_sample(d3s_ctx *ctx, const void *h_dev, int64_t ld_h, const void *W_dev,
+                      int64_t ld_w, int D, const d3s_request *req, void *stream) {
+  if (!ctx || !req) return fail(D3S_ERR_ARG, "null ctx or request");
+  if (req->dtype != D3S_BF16) return fail(D3S_ERR_ARG, "the projection writes bf16 logits");
+  int rc = d3s_lmhead(ctx, h_dev, ld_h, W_dev, ld_w, req->N, req->V, D,
+                      const_cast<void *>(req->logits), req->ld, stream);
+  if (rc != D3S_OK) return rc;
+  return d3s_sample(ctx, req, stream);
+}
+
 // ---- the test ABI of the reference ----
 
 static std::mutex g_default_mu;

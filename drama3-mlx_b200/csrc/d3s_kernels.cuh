@@ -96,6 +96,22 @@ struct FrameScratch {
 // `a` carries the logits (logits, dtype, V, ld) and the scratch pointers.
 int launch_frame(const FrameArgs &f, const FrameScratch &fs, KArgs a, const Scratch &sc,
                  cudaStream_t stream);
+// The lm_head projection: out[b, v] = bf16(h[b, :] . W[v, :]), fp32 accumulate.
+// h [B, D], W [V, D], out [B, ld_out], all bf16 device memory, rows 16-byte
+// aligned (ld and D multiples of 8).
+constexpr int kGemvMaxB = 8;  // batch rows up to which the CUDA-core GEMV runs
+struct LmArgs {
+  const void *h;
+  int64_t ld_h;
+  const void *W;
+  int64_t ld_w;
+  int B, V, D;
+  void *out;
+  int64_t ld_out;
+  int32_t *error;  // bit 1 set when a bounded wait in the GEMM gave up
+};
+int launch_lmhead(const LmArgs &a, cudaStream_t stream);
+
 // Advance S key states by n splits each; subkeys at sub[s * ld_sub + i].
 int launch_keys_next(uint2 *state, int S, int n, uint2 *sub, int64_t ld_sub, cudaStream_t stream);
 

@@ -1,0 +1,402 @@
+// d3s_lmhead.cu - the restricted lm_head projection in front of the sampler:
+// logits[b, v] = bf16(sum_d h[b, d] * W[v, d]) with fp32 accumulation, the
+// bf16 output of backbone_audio_logits -> m_linear -> gemv_row
+// (src/backbone.c:1213, src/mlxu.c:397, src/mlxu.c:442-496).
+//
+// Two kernels:
+//   * B <= kGemvMaxB: a CUDA-core GEMV. One warp per W row, 16-byte loads of
+//     the row, h staged once per CTA in shared memory; it streams W once
+//     (16.8 MB for the backbone's [4097, 2048]) and is HBM-bound.
+//   * larger B: a tcgen05 GEMM with the operands swapped so that the long
+//     side (V logit ids) is the UMMA M dimension: D[v, b] = W[v, :] . h[b, :].
+//     Tiles of 128 W rows x BN batch rows, K staged 64 at a time by TMA
+//     (128-byte swizzle) through a ring of shared-memory stages; one thread
+//     issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32 in TMEM) and commits
+//     each stage back to the producer; four epilogue warps read the
+//     accumulator with tcgen05.ld, round to bf16 and store logits[b, v].
+//     No clusters and no multicast: every CTA loads its own tiles.
+// Every wait on an mbarrier is bounded (kLmWaitLimitNs); a wait that gives up
+// sets the error word and the kernel drains its copies, frees its tensor
+// memory and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
+#include "d3s.h"
+#include "d3s_device.cuh"
+#include "d3s_kernels.cuh"
+
+namespace d3s {
+namespace {
+
+constexpr int kGemvWarps = 8;
+constexpr int kBM = 128;           // W rows per tile (UMMA M)
+constexpr int kBK = 64;            // K per stage: one 128-byte swizzle row of bf16
+constexpr int kUK = 16;            // K per tcgen05.mma of kind::f16
+constexpr int kGemmThreads = 192;  // warp 0: TMA, warp 1: TMEM + MMA, warps 2-5: epilogue
+constexpr uint64_t kLmWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t saddr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void bar_init(uint64_t *b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false when it gave up or another role already gave up.
+__device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+  if (bar_try(b, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  while (!bar_try(b, parity)) {
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > kLmWaitLimitNs) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(saddr(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(saddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the
+// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO),
+// leading offset 1 (unused for swizzled K-major), descriptor version 1,
+// layout type 2 (SWIZZLE_128B). The tile base is 1024-byte aligned, so the
+// base offset is 0; a K step inside the swizzle row adds its byte offset to
+// the start address.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and B
+// bf16 (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
+// bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          saddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN>
+struct GemmCfg {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+  static constexpr uint32_t kTmemCols = BN <= 32 ? 32 : BN;  // a power of two >= 32
+  // stages, then 2 * stages + 1 mbarriers, the TMEM address and the abort flag,
+  // plus slack to align the base to 1024
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + (2 * kStages + 1) * 8 + 16 + 1024;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M = 128");
+  static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte alignment of the swizzle");
+  static_assert((kTmemCols & (kTmemCols - 1)) == 0, "TMEM columns: a power of two");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    lmhead_gemm_kernel(const __grid_constant__ CUtensorMap tmW,
+                       const __grid_constant__ CUtensorMap tmH, __nv_bfloat16 *out,
+                       int64_t ld_out, int V, int B, int KT, int32_t *error) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ unsigned char dsmem[];
+  unsigned char *base =
+      (unsigned char *)(((uintptr_t)dsmem + 1023) & ~(uintptr_t)1023);  // swizzle atoms: 1024-aligned
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + (size_t)S * Cfg::kStageBytes);
+  uint64_t *empty = full + S;
+  uint64_t *accum = empty + S;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM;  // first W row (logit id) of the tile
+  const int n0 = blockIdx.y * BN;   // first batch row of the tile
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    bar_init(accum, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(Cfg::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // producer: W tile [128 x 64] and h tile [BN x 64] per stage
+    int issued = 0;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % S;
+      if (kt >= S && !bar_wait(&empty[s], ((kt / S) & 1) ^ 1, abort_flag)) break;
+      unsigned char *st = base + (size_t)s * Cfg::kStageBytes;
+      bar_expect_tx(&full[s], Cfg::kStageBytes);
+      tma_load_2d(st, &tmW, kt * kBK, m0, &full[s]);
+      tma_load_2d(st + Cfg::kABytes, &tmH, kt * kBK, n0, &full[s]);
+      ++issued;
+    }
+    if (*abort_flag) {  // let the copies still in flight land before the CTA exits
+      for (int kt = issued - S > 0 ? issued - S : 0; kt < issued; ++kt) {
+        const unsigned long long t0 = now_ns();
+        while (!bar_try(&full[kt % S], (kt / S) & 1) && now_ns() - t0 < kLmWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    constexpr uint32_t idesc = umma_idesc(kBM, BN);
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % S;
+      if (!bar_wait(&full[s], (kt / S) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t a0 = saddr(base + (size_t)s * Cfg::kStageBytes);
+      const uint32_t b0 = a0 + Cfg::kABytes;
+#pragma unroll
+      for (int kk = 0; kk < kBK / kUK; ++kk)
+        umma_bf16(tmem, sw128_desc(a0 + kk * kUK * 2), sw128_desc(b0 + kk * kUK * 2), idesc,
+                  (kt | kk) != 0 ? 1u : 0u);
+      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+    }
+    umma_commit(accum);  // arrives when every MMA issued above is complete
+  } else if (warp >= 2) {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = W rows of the tile
+    const int q = warp & 3;
+    const bool ok = bar_wait(accum, 0, abort_flag);
+    tc_fence_after();
+    const int v = m0 + q * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+      if (ok && !*abort_flag && v < V) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int b = n0 + c + j;
+          if (b < B) out[(int64_t)b * ld_out + v] = __float2bfloat16_rn(__uint_as_float(r[j]));
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Cfg::kTmemCols)
+                 : "memory");
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(error, 2);
+}
+
+// ---- GEMV (B <= kGemvMaxB) ----
+
+template <int NB>
+__global__ void __launch_bounds__(32 * kGemvWarps)
+    lmhead_gemv_kernel(const __nv_bfloat16 *h, int64_t ld_h, const __nv_bfloat16 *W,
+                       int64_t ld_w, int B, int V, int D, __nv_bfloat16 *out, int64_t ld_out) {
+  extern __shared__ __align__(16) unsigned char hs_raw[];
+  __nv_bfloat16 *hs = reinterpret_cast<__nv_bfloat16 *>(hs_raw);  // [NB][D]
+  const int chunks = D >> 3;                                       // 16-byte chunks per row
+  for (int i = threadIdx.x; i < NB * chunks; i += blockDim.x) {
+    const int b = i / chunks, c = i - b * chunks;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (b < B) v = *reinterpret_cast<const uint4 *>(h + (int64_t)b * ld_h + 8 * c);
+    reinterpret_cast<uint4 *>(hs)[i] = v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+  for (int v = gw; v < V; v += nw) {
+    const uint4 *wr = reinterpret_cast<const uint4 *>(W + (int64_t)v * ld_w);
+    float acc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
+#pragma unroll 4
+    for (int c = lane; c < chunks; c += 32) {
+      const uint4 w4 = __ldg(wr + c);
+      const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w4);
+      float wf[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(w2[e]);
+        wf[2 * e] = f.x;
+        wf[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const uint4 h4 = reinterpret_cast<const uint4 *>(hs)[b * chunks + c];
+        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&h4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h2[e]);
+          acc[b] = __fmaf_rn(wf[2 * e], f.x, acc[b]);
+          acc[b] = __fmaf_rn(wf[2 * e + 1], f.y, acc[b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[b] = __fadd_rn(acc[b], __shfl_xor_sync(0xffffffffu, acc[b], o));
+    }
+    if (lane < NB && lane < B) {
+      float mine = acc[0];
+#pragma unroll
+      for (int b = 1; b < NB; ++b)
+        if (lane == b) mine = acc[b];
+      out[(int64_t)lane * ld_out + v] = __float2bfloat16_rn(mine);
+    }
+  }
+}
+
+// ---- host: tensor maps ----
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 matrix [rows, cols] with row stride ld (elements), box [box_rows, 64].
+bool make_map(CUtensorMap *m, const void *ptr, int rows, int cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+int launch_gemm(const LmArgs &a, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap tw, th;
+  if (!make_map(&tw, a.W, a.V, a.D, a.ld_w, kBM) || !make_map(&th, a.h, a.B, a.D, a.ld_h, BN))
+    return D3S_ERR_CUDA;
+  if (cudaFuncSetAttribute(lmhead_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)Cfg::kSmem) != cudaSuccess)
+    return D3S_ERR_CUDA;
+  const dim3 grid((a.V + kBM - 1) / kBM, (a.B + BN - 1) / BN);
+  const int KT = (a.D + kBK - 1) / kBK;
+  lmhead_gemm_kernel<BN><<<grid, kGemmThreads, Cfg::kSmem, st>>>(
+      tw, th, reinterpret_cast<__nv_bfloat16 *>(a.out), a.ld_out, a.V, a.B, KT, a.error);
+  return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+}
+
+template <int NB>
+int launch_gemv(const LmArgs &a, cudaStream_t st) {
+  const size_t smem = (size_t)NB * a.D * 2;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(lmhead_gemv_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return D3S_ERR_CUDA;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = std::max(1, std::min((a.V + kGemvWarps - 1) / kGemvWarps, 2 * sms));
+  lmhead_gemv_kernel<NB><<<blocks, 32 * kGemvWarps, smem, st>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(a.h), a.ld_h,
+      reinterpret_cast<const __nv_bfloat16 *>(a.W), a.ld_w, a.B, a.V, a.D,
+      reinterpret_cast<__nv_bfloat16 *>(a.out), a.ld_out);
+  return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+}
+
+}  // namespace
+
+int launch_lmhead(const LmArgs &a, cudaStream_t st) {
+  if (a.B == 0 || a.V == 0) return D3S_OK;
+  if (a.B <= 1) return launch_gemv<1>(a, st);
+  if (a.B <= 2) return launch_gemv<2>(a, st);
+  if (a.B <= 4) return launch_gemv<4>(a, st);
+  if (a.B <= kGemvMaxB) return launch_gemv<kGemvMaxB>(a, st);
+  if (a.B <= 32) return launch_gemm<32>(a, st);
+  if (a.B <= 64) return launch_gemm<64>(a, st);
+  if (a.B <= 128) return launch_gemm<128>(a, st);
+  return launch_gemm<256>(a, st);
+}
+
+}  // namespace d3s

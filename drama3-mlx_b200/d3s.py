@@ -40,7 +40,8 @@ EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split"
            "d3s_next_key", "d3s_ctx_create", "d3s_ctx_destroy", "d3s_ctx_reserve",
            "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
            "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3s_sample_rows_static",
-           "d3_sample", "d3s_last_status", "d3s_keys_next", "d3s_frame_main")
+           "d3_sample", "d3s_last_status", "d3s_keys_next", "d3s_frame_main", "d3s_lmhead",
+           "d3s_lmhead_sample")
 RAS_WINDOW = 16
 FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
 STATIC_MAX_ROWS = 4096
@@ -133,6 +134,8 @@ def lib() -> ctypes.CDLL:
         L.d3s_last_status.restype = i32
         L.d3s_keys_next.argtypes = [vp, vp, i32, i32, vp, i64, vp]
         L.d3s_frame_main.argtypes = [vp, ctypes.POINTER(FrameRequest), vp]
+        L.d3s_lmhead.argtypes = [vp, vp, i64, vp, i64, i32, i32, i32, vp, i64, vp]
+        L.d3s_lmhead_sample.argtypes = [vp, vp, i64, vp, i64, i32, ctypes.POINTER(Request), vp]
         _lib = L
     return _lib
 
@@ -379,6 +382,24 @@ class Context:
         f.main_tok, f.c0, f.flags = _ptr(main_tok), _ptr(c0), _ptr(flags)
         _check(lib().d3s_frame_main(self._h, ctypes.byref(f), _stream_ptr(stream)))
         return main_tok, c0, flags
+
+    def lmhead(self, h, W, out=None, stream=None):
+        """logits [B, V] bf16 = bf16(h [B, D] @ W [V, D]^T), fp32 accumulation."""
+        import torch
+        B, D = h.shape
+        V = W.shape[0]
+        if out is None:
+            out = torch.empty(B, V, dtype=torch.bfloat16, device=h.device)
+        _check(lib().d3s_lmhead(self._h, _ptr(h), h.stride(0), _ptr(W), W.stride(0), B, V, D,
+                                _ptr(out), out.stride(0), _stream_ptr(stream)))
+        return out
+
+    def lmhead_sample(self, h, W, logits, ids, stream=None, **request):
+        """d3s_lmhead into `logits` (bf16 [B, V]) then d3s_sample; keyword
+        arguments as for request()."""
+        req = self.request(logits, ids, **request)
+        _check(lib().d3s_lmhead_sample(self._h, _ptr(h), h.stride(0), _ptr(W), W.stride(0),
+                                       h.shape[1], ctypes.byref(req), _stream_ptr(stream)))
 
     def check(self) -> None:
         """Synchronise and raise if a kernel recorded a failure (a bounded wait)."""

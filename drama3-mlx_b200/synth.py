@@ -64,6 +64,15 @@ def c4_logits(rows: int, seed: int, device="cuda", V: int = 1024,
     return x.to(torch.bfloat16)
 
 
+def c3_inputs(B: int, seed: int = 0, device="cuda", V: int = 4097, D: int = 2048):
+    """(h bf16 [B, D] ~ N(0, 1), W bf16 [V, D] ~ N(0, 0.02)): the hidden states
+    and the restricted lm_head weight of the fused-prologue config."""
+    g = _gen(seed, device)
+    h = torch.randn(B, D, generator=g, device=device).to(torch.bfloat16)
+    W = (torch.randn(V, D, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return h, W
+
+
 def c5_batch(N: int = 65536, seed: int = 0, device="cuda", V: int = 4097):
     """(logits f32 [N, V], temperature [N], top_p [N], top_k int32 [N], seeds int64 [N])."""
     g = _gen(seed, device)

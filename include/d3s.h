@@ -231,6 +231,26 @@ typedef struct {
  * keys = sub + 2 + j, ld_keys = n. */
 D3S_API int d3s_frame_main(d3s_ctx *ctx, const d3s_frame_request *req, void *stream);
 
+/* ---- the lm_head projection in front of the sampler ---- */
+
+/* backbone_audio_logits -> m_linear (src/backbone.c:1213, src/mlxu.c:442-496):
+ * logits_dev[b, v] = bf16(sum_d h_dev[b, d] * W_dev[v, d]) with fp32
+ * accumulation and a round-to-nearest bf16 result, as the reference's GEMV
+ * writes bf16 logits (src/mlxu.c:397). h [B, D], W [V, D] (the restricted
+ * lm_head_audio [4097, 2048], src/model.h:71) and logits [B, ld_logits] are
+ * bf16 device arrays with 16-byte aligned rows (D, ld_h, ld_w multiples of 8).
+ * B <= 8 runs a CUDA-core GEMV; larger B a tcgen05 tensor-core GEMM. The sum
+ * order differs from MLX's, so logits can differ from the reference's by one
+ * bf16 rounding step where the fp32 sum lies next to a rounding boundary. */
+D3S_API int d3s_lmhead(d3s_ctx *ctx, const void *h_dev, int64_t ld_h, const void *W_dev,
+                       int64_t ld_w, int B, int V, int D, void *logits_dev, int64_t ld_logits,
+                       void *stream);
+
+/* The fused prologue: d3s_lmhead into req->logits (bf16, [req->N = B,
+ * req->ld], V = req->V), then d3s_sample(req) on the same stream. */
+D3S_API int d3s_lmhead_sample(d3s_ctx *ctx, const void *h_dev, int64_t ld_h, const void *W_dev,
+                              int64_t ld_w, int D, const d3s_request *req, void *stream);
+
 /* ---- the reference's test C-ABI (src/testapi.c:155-166) ---- */
 
 /* Host logits [N, V] f32 -> host ids [N]: seeds the global key with `seed`,

@@ -1,0 +1,100 @@
+"""The lm_head projection (d3s_lmhead) and the fused prologue
+(d3s_lmhead_sample) on the GPU.
+
+The projection's fp32 sum runs in a different order from MLX's (and from
+torch's), so the logits are checked against a float64 reference within the
+bound that bf16 rounding plus fp32 accumulation allows:
+|logit - ref| <= 2^-8 |ref| + 1e-4 for h ~ N(0, 1), W ~ N(0, 0.02), D = 2048
+(the fp32 sum's error is ~1e-5 absolute there), and at least 99% of them
+must equal torch's own bf16 result. The sampled ids must equal the oracle's
+sampling of the projection's own bf16 logits bit for bit."""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not torch.cuda.is_available():
+        pytest.fail("the gpu tests need a CUDA device")
+    import d3s
+    c = d3s.Context(0)
+    yield c
+    c.close()
+
+
+def check_logits(out, h, W):
+    ref64 = h.double() @ W.double().T
+    o = out.double()
+    err = (o - ref64).abs()
+    bound = ref64.abs() * 2.0**-8 + 1e-4
+    assert bool((err <= bound).all()), float((err - bound).max())
+    tref = (h.float() @ W.float().T).to(torch.bfloat16)
+    same = (out.view(torch.int16) == tref.view(torch.int16)).float().mean().item()
+    assert same >= 0.99, same
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 5, 8, 9, 16, 33, 64, 100, 128, 200, 256, 1024])
+def test_projection_c3(ctx, B):
+    import synth
+    h, W = synth.c3_inputs(B, seed=B)
+    out = ctx.lmhead(h, W)
+    torch.cuda.synchronize()
+    ctx.check()
+    check_logits(out, h, W)
+
+
+@pytest.mark.parametrize("B,V,D", [(1, 1024, 256), (7, 300, 64), (64, 1024, 1024), (40, 4097, 2056),
+                                   (300, 129, 512)])
+def test_projection_shapes(ctx, B, V, D):
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + V)
+    h = torch.randn(B, D, generator=g, device="cuda").to(torch.bfloat16)
+    W = (torch.randn(V, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    out = ctx.lmhead(h, W)
+    ctx.check()
+    check_logits(out, h, W)
+
+
+def test_projection_strided_output(ctx):
+    import synth
+    B, V = 70, 4097
+    h, W = synth.c3_inputs(B, seed=3)
+    big = torch.full((B, V + 31), 7.0, dtype=torch.bfloat16, device="cuda")
+    out = big[:, :V]
+    ctx.lmhead(h, W, out=out)
+    ctx.check()
+    check_logits(out, h, W)
+    assert bool((big[:, V:] == 7.0).all())
+
+
+@pytest.mark.parametrize("B", [1, 64, 1024])
+def test_lmhead_sample_matches_oracle_on_its_logits(ctx, oracle, B):
+    import d3s
+    import synth
+    h, W = synth.c3_inputs(B, seed=100 + B)
+    V = W.shape[0]
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device="cuda")
+    ids = torch.empty(B, dtype=torch.int32, device="cuda")
+    seeds = torch.arange(B, dtype=torch.int64, device="cuda") + 555
+    ctx.lmhead_sample(h, W, logits, ids, temperature=0.7, top_p=0.7, top_k=30,
+                      noise=d3s.NOISE_SEEDS, seeds=seeds)
+    torch.cuda.synchronize()
+    ctx.check()
+    want = oracle.sample_rows(synth.to_host_logits(logits), 0.7, 0.7, 30, seeds.cpu().numpy())
+    np.testing.assert_array_equal(ids.cpu().numpy(), want)
+    check_logits(logits, h, W)
+
+
+def test_lmhead_rejects_bad_arguments(ctx):
+    import d3s
+    h = torch.zeros(4, 2048, dtype=torch.bfloat16, device="cuda")
+    W = torch.zeros(4097, 2048, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(d3s.D3SError):
+        ctx.lmhead(h[:, 1:], W[:, 1:])  # rows not 16-byte aligned
+    with pytest.raises(d3s.D3SError):
+        ctx.lmhead(torch.zeros(4, 12, dtype=torch.bfloat16, device="cuda"),
+                   torch.zeros(9, 12, dtype=torch.bfloat16, device="cuda"))  # D % 8

@@ -258,62 +258,101 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // ---- GEMV (B <= kGemvMaxB) ----
 
+constexpr int kGemvRows = 2;   // W rows per warp task
+constexpr int kGemvGroup = 8;  // 16-byte chunks per lane per pass (D = 2048: one pass)
+
+template <int NB>
+__device__ __forceinline__ void gemv_load(uint4 (&w)[kGemvRows][kGemvGroup], const __nv_bfloat16 *W,
+                                          int64_t ld_w, int V, int chunks, int v0, int g,
+                                          int lane) {
+#pragma unroll
+  for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+    for (int i = 0; i < kGemvGroup; ++i) {
+      const int c = g + lane + 32 * i;
+      w[r][i] = (v0 + r < V && c < chunks)
+                    ? __ldg(reinterpret_cast<const uint4 *>(W + (int64_t)(v0 + r) * ld_w) + c)
+                    : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// One warp per pair of W rows; each lane holds 8 16-byte chunks of both rows
+// (all loads issued before any use, the first task's before h is staged), h
+// is read from shared memory, the fp32 sums are reduced across the warp.
 template <int NB>
 __global__ void __launch_bounds__(32 * kGemvWarps)
     lmhead_gemv_kernel(const __nv_bfloat16 *h, int64_t ld_h, const __nv_bfloat16 *W,
                        int64_t ld_w, int B, int V, int D, __nv_bfloat16 *out, int64_t ld_out) {
   extern __shared__ __align__(16) unsigned char hs_raw[];
-  __nv_bfloat16 *hs = reinterpret_cast<__nv_bfloat16 *>(hs_raw);  // [NB][D]
-  const int chunks = D >> 3;                                       // 16-byte chunks per row
+  const uint4 *hs = reinterpret_cast<const uint4 *>(hs_raw);  // [NB][chunks]
+  const int chunks = D >> 3;                                   // 16-byte chunks per row
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+  int v0 = gw * kGemvRows;
+  uint4 w[kGemvRows][kGemvGroup];
+  if (v0 < V) gemv_load<NB>(w, W, ld_w, V, chunks, v0, 0, lane);
   for (int i = threadIdx.x; i < NB * chunks; i += blockDim.x) {
     const int b = i / chunks, c = i - b * chunks;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (b < B) v = *reinterpret_cast<const uint4 *>(h + (int64_t)b * ld_h + 8 * c);
-    reinterpret_cast<uint4 *>(hs)[i] = v;
+    reinterpret_cast<uint4 *>(hs_raw)[i] = v;
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
-  for (int v = gw; v < V; v += nw) {
-    const uint4 *wr = reinterpret_cast<const uint4 *>(W + (int64_t)v * ld_w);
-    float acc[NB];
+  for (; v0 < V; v0 += nw * kGemvRows) {
+    float acc[kGemvRows][NB];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
-#pragma unroll 4
-    for (int c = lane; c < chunks; c += 32) {
-      const uint4 w4 = __ldg(wr + c);
-      const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w4);
-      float wf[8];
+    for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(w2[e]);
-        wf[2 * e] = f.x;
-        wf[2 * e + 1] = f.y;
-      }
+      for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
+    for (int g = 0; g < chunks; g += 32 * kGemvGroup) {
+      if (g > 0) gemv_load<NB>(w, W, ld_w, V, chunks, v0, g, lane);
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        const uint4 h4 = reinterpret_cast<const uint4 *>(hs)[b * chunks + c];
-        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&h4);
+      for (int i = 0; i < kGemvGroup; ++i) {
+        const int c = g + lane + 32 * i;
+        if (c >= chunks) break;
+        float wf[kGemvRows][8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(h2[e]);
-          acc[b] = __fmaf_rn(wf[2 * e], f.x, acc[b]);
-          acc[b] = __fmaf_rn(wf[2 * e + 1], f.y, acc[b]);
+        for (int r = 0; r < kGemvRows; ++r) {
+          const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w[r][i]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(w2[e]);
+            wf[r][2 * e] = f.x;
+            wf[r][2 * e + 1] = f.y;
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const uint4 h4 = hs[b * chunks + c];
+          const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&h4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h2[e]);
+#pragma unroll
+            for (int r = 0; r < kGemvRows; ++r) {
+              acc[r][b] = __fmaf_rn(wf[r][2 * e], f.x, acc[r][b]);
+              acc[r][b] = __fmaf_rn(wf[r][2 * e + 1], f.y, acc[r][b]);
+            }
+          }
         }
       }
     }
+    const int vn = v0 + nw * kGemvRows;
+    if (vn < V) gemv_load<NB>(w, W, ld_w, V, chunks, vn, 0, lane);  // next task's loads in flight
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
+    for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[b] = __fadd_rn(acc[b], __shfl_xor_sync(0xffffffffu, acc[b], o));
-    }
-    if (lane < NB && lane < B) {
-      float mine = acc[0];
+      for (int b = 0; b < NB; ++b)
 #pragma unroll
-      for (int b = 1; b < NB; ++b)
-        if (lane == b) mine = acc[b];
-      out[(int64_t)lane * ld_out + v] = __float2bfloat16_rn(mine);
-    }
+        for (int o = 16; o > 0; o >>= 1)
+          acc[r][b] = __fadd_rn(acc[r][b], __shfl_xor_sync(0xffffffffu, acc[r][b], o));
+    // lane r * NB + b writes (row v0 + r, batch b)
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        if (lane == r * NB + b && b < B && v0 + r < V)
+          out[(int64_t)b * ld_out + v0 + r] = __float2bfloat16_rn(acc[r][b]);
   }
 }
 
@@ -377,7 +416,8 @@ int launch_gemv(const LmArgs &a, cudaStream_t st) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int blocks = std::max(1, std::min((a.V + kGemvWarps - 1) / kGemvWarps, 2 * sms));
+  const int tasks = (a.V + kGemvRows - 1) / kGemvRows;
+  const int blocks = std::max(1, std::min((tasks + kGemvWarps - 1) / kGemvWarps, 4 * sms));
   lmhead_gemv_kernel<NB><<<blocks, 32 * kGemvWarps, smem, st>>>(
       reinterpret_cast<const __nv_bfloat16 *>(a.h), a.ld_h,
       reinterpret_cast<const __nv_bfloat16 *>(a.W), a.ld_w, a.B, a.V, a.D,

@@ -749,6 +749,51 @@ __device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k,
   }
 }
 
+// In place in shared memory: sort the C <= 32 S keys of list[] and leave the
+// first k in rank order at list[0..k).
+template <int S>
+__device__ __forceinline__ void sort_list(unsigned long long *list, int C, int k, int lane) {
+  unsigned long long v[S];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const int e = lane + 32 * s;
+    v[s] = e < C ? list[e] : 0ull;
+  }
+  warp_sort_desc<S>(v, lane);
+  __syncwarp();
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+    if (lane + 32 * s < k) list[lane + 32 * s] = v[s];
+}
+
+// In place: the k largest of C <= 256 keys, one per round, into list[0..k).
+__device__ __forceinline__ void select_list(unsigned long long *list, int C, int k, int lane) {
+  unsigned long long v[8], best = 0ull;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const int e = lane + 32 * s;
+    v[s] = e < C ? list[e] : 0ull;
+    best = v[s] > best ? v[s] : best;
+  }
+  __syncwarp();
+  for (int r = 0; r < k; ++r) {
+    const unsigned mh = __reduce_max_sync(kFull, (unsigned)(best >> 32));
+    const unsigned ml =
+        __reduce_max_sync(kFull, (unsigned)(best >> 32) == mh ? (unsigned)best : 0u);
+    const unsigned long long wk = ((unsigned long long)mh << 32) | ml;
+    if (best == wk) {
+      unsigned long long nb = 0ull;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (v[s] == wk) v[s] = 0ull;
+        nb = v[s] > nb ? v[s] : nb;
+      }
+      best = nb;
+    }
+    if (lane == 0) list[r] = wk;
+  }
+}
+
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
                : "memory");
@@ -846,6 +891,302 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
     }
     raw = rawn;
     cnt_next = cnt_nn;
+  }
+}
+
+// ---- row-warp kernel: one warp takes a row from its logits to its draw ----
+//
+// Each warp owns a shared-memory stage holding one row (one bulk copy of the
+// 16-byte-aligned span around it; the row starts s elements into the stage)
+// plus a candidate list and scratch. Lane l reads the stage's 16-byte chunks
+// l, l + 32, ..., l + 32 (NC - 1). Chunk c, component e is element
+// EPC c + e - s (EPC = 4 for f32, 8 for bf16), so a lane always meets the
+// elements of the same eight partials (element i belongs to partial
+// i mod 256), each in increasing order: f32 lane l holds partials
+// 4l + e - s + 128 (i & 1), bf16 lane l holds 8l + e - s (mod 256).
+//   pass 1: max, min, and four group maxima per lane (chunk i in group i % 4);
+//   threshold: min over the groups of the ceil(k/4)-th largest of the 32 lanes'
+//     group maxima (every group contributes >= ceil(k/4) elements at or above
+//     it, so >= k elements reach it);
+//   pass 2: q = x / T, the lane's eight partial sums of exp(max(q - max, -86))
+//     as packed fp32x2 chains, and a bit per element with q >= threshold;
+//   then the candidates go to the warp's list, the next row's copy starts into
+//   the stage, and the warp sorts the candidates and runs the tail.
+// Rows it cannot finish (k > 256, more than 256 candidates) go to the
+// hand-off list for the wide kernel.
+
+constexpr int kRwCandBytes = kCandCap * 8;
+constexpr int kRwScrBytes = (kFastMaxK + 4) * 4;
+constexpr int kRwTailBytes = kRwCandBytes + kRwScrBytes + 16;  // + the mbarrier
+constexpr int kRowWarpMaxBatch = 2048;  // long rows: batches up to this take the row-warp kernel
+
+// min over four 32-lane columns (v[c] of every lane) of each column's r-th
+// largest value (1 <= r <= 32): four interleaved bitonic sorts.
+__device__ __forceinline__ float warp_tau4(float (&v)[4], int r, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float o = __shfl_xor_sync(kFull, v[c], stride);
+        v[c] = keep_max ? fmaxf(v[c], o) : fminf(v[c], o);
+      }
+    }
+  float t = __shfl_sync(kFull, v[0], r - 1);
+#pragma unroll
+  for (int c = 1; c < 4; ++c) t = fminf(t, __shfl_sync(kFull, v[c], r - 1));
+  return t;
+}
+
+// One 16-byte chunk of the stage as floats.
+template <bool BF16>
+__device__ __forceinline__ void rw_chunk(const unsigned char *stage, int c,
+                                         float (&x)[BF16 ? 8 : 4]) {
+  const uint4 u = *reinterpret_cast<const uint4 *>(stage + 16 * (size_t)c);
+  if constexpr (BF16) {
+    const unsigned w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      x[2 * j] = __uint_as_float(w[j] << 16);
+      x[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  } else {
+    x[0] = __uint_as_float(u.x);
+    x[1] = __uint_as_float(u.y);
+    x[2] = __uint_as_float(u.z);
+    x[3] = __uint_as_float(u.w);
+  }
+}
+
+// Pass 2 over the lane's chunks. FAST: the per-row reciprocal division holds
+// for every element; CLAMP: some term may fall below the -86 floor.
+template <int NC, bool BF16, bool FAST, bool CLAMP>
+__device__ __forceinline__ void rw_pass2(const unsigned char *stage, int lane, int s, int V,
+                                         int cfull, float T, float rT, float gmax, float tau,
+                                         float2 (&acc)[4],
+                                         unsigned long long (&bits)[(NC * (BF16 ? 8 : 4) + 63) / 64]) {
+  constexpr int EPC = BF16 ? 8 : 4;
+  const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-T, -T);
+  const float2 mg = make_float2(-gmax, -gmax);
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = lane + 32 * i;
+    float x[EPC];
+    rw_chunk<BF16>(stage, c, x);
+    const bool partial = i == 0 || 32 * i + 31 >= cfull;  // warp-uniform
+#pragma unroll
+    for (int pp = 0; pp < EPC / 2; ++pp) {
+      float2 q;
+      if (FAST) {
+        q = div_rows2(make_float2(x[2 * pp], x[2 * pp + 1]), rT2, mT2);
+      } else {
+        q = make_float2(__fdiv_rn(x[2 * pp], T), __fdiv_rn(x[2 * pp + 1], T));
+      }
+      float2 e = exp_term2<CLAMP>(__fadd2_rn(q, mg));
+      bool v0 = true, v1 = true;
+      if (partial) {
+        const int p0 = EPC * c + 2 * pp;
+        v0 = p0 >= s && p0 < V + s;
+        v1 = p0 + 1 >= s && p0 + 1 < V + s;
+        if (!v0) e.x = 0.0f;
+        if (!v1) e.y = 0.0f;
+      }
+      const int ai = BF16 ? pp : 2 * (i & 1) + pp;
+      acc[ai] = __fadd2_rn(acc[ai], e);
+      const int b = i * EPC + 2 * pp;
+      if (v0 && q.x >= tau) bits[b >> 6] |= 1ull << (b & 63);
+      if (v1 && q.y >= tau) bits[(b + 1) >> 6] |= 1ull << ((b + 1) & 63);
+    }
+  }
+}
+
+// Sum over the warp of each lane's fixed-point total (< 2^55): three 21/21/22-bit
+// pieces, each summed exactly by a 32-bit redux.
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+  const unsigned p0 = __reduce_add_sync(kFull, (unsigned)(v & 0x1FFFFFu));
+  const unsigned p1 = __reduce_add_sync(kFull, (unsigned)((v >> 21) & 0x1FFFFFu));
+  const unsigned p2 = __reduce_add_sync(kFull, (unsigned)(v >> 42));
+  return (unsigned long long)p0 + ((unsigned long long)p1 << 21) + ((unsigned long long)p2 << 42);
+}
+
+// Warps that fit on an SM: the f32 rows of the largest chunk counts are held
+// back by shared memory (about 20 KB a warp), so they may use more registers.
+template <int NC>
+struct RwBounds {
+  static constexpr int kMinBlocks = NC >= 25 ? 10 : 16;
+};
+
+template <int NC, bool BF16>
+__global__ void __launch_bounds__(32, RwBounds<NC>::kMinBlocks)
+    sample_rowwarp_kernel(const KArgs a, int stage_bytes) {
+  extern __shared__ __align__(128) unsigned char dsm[];
+  constexpr int ESZ = BF16 ? 2 : 4;
+  constexpr int EPC = 16 / ESZ;
+  constexpr int NBW = (NC * EPC + 63) / 64;
+  const int lane = threadIdx.x;
+  unsigned char *stage = dsm;
+  unsigned long long *cs = reinterpret_cast<unsigned long long *>(dsm + stage_bytes);
+  float *scr = reinterpret_cast<float *>(dsm + stage_bytes + kRwCandBytes);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(dsm + stage_bytes + kRwCandBytes + kRwScrBytes);
+  const int V = a.V;
+  const uint64_t pol = evict_first_policy();
+  if (lane == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  int row = blockIdx.x;
+  const int nrows = gridDim.x;
+  if (row < a.N && lane == 0) issue_row<ESZ>(a, row, stage, bar, pol);
+  RawP nxt;
+  if (row < a.N) nxt = load_raw(a, row);
+  uint32_t phase = 0;
+  for (; row < a.N; row += nrows, phase ^= 1u) {
+    const RawP cur = nxt;
+    const int nrow = row + nrows;
+    if (nrow < a.N) nxt = load_raw(a, nrow);
+    RowP rp;
+    const int pst = resolve(a, cur, rp);
+    if (!mbar_wait_bounded(bar, phase)) {
+      if (lane == 0) {
+        atomicOr(a.error, 1);
+        mbar_wait_bounded(bar, phase);  // let the copy in flight land before exiting
+      }
+      return;
+    }
+    const int s = (int)((((uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ) &
+                         15) / ESZ);
+    const int cfull = (V + s) / EPC;  // chunks 1 .. cfull - 1 lie inside the row
+
+    // pass 1: max, min, group maxima
+    float pm[4] = {-f_inf(), -f_inf(), -f_inf(), -f_inf()};
+    float mn0 = f_inf(), mn1 = f_inf();
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      float x[EPC];
+      rw_chunk<BF16>(stage, c, x);
+      if (i == 0 || 32 * i + 31 >= cfull) {
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+          const int p = EPC * c + e;
+          const bool valid = p >= s && p < V + s;
+          pm[i & 3] = max_nan(pm[i & 3], valid ? x[e] : -f_inf());
+          if (e & 1)
+            mn1 = fminf(mn1, valid ? x[e] : f_inf());
+          else
+            mn0 = fminf(mn0, valid ? x[e] : f_inf());
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+          pm[i & 3] = max_nan(pm[i & 3], x[e]);
+          if (e & 1)
+            mn1 = fminf(mn1, x[e]);
+          else
+            mn0 = fminf(mn0, x[e]);
+        }
+      }
+    }
+    const float xmax = warp_max_nan(max_nan(max_nan(pm[0], pm[1]), max_nan(pm[2], pm[3])));
+    const float xmin = -warp_max(-fminf(mn0, mn1));
+    if (a.finite && lane == 0) a.finite[row] = (fabsf(xmax) < f_inf() && fabsf(xmin) < f_inf()) ? 1 : 0;
+
+    bool go = false;
+    float lse = 0.0f;
+    int C = 0;
+    if (pst != D3S_ROW_OK) {
+      if (lane == 0) flag_row(a, row, pst);
+    } else if (rp.k > kFastMaxK) {
+      if (lane == 0) defer_row(a, row);
+    } else {
+      const float T = rp.T;
+      const float gmax = __fdiv_rn(xmax, T);  // max(x / T) = RN(max(x) / T): RN is monotone
+      if (!(fabsf(gmax) < f_inf())) {         // NaN, +inf, or every value -inf
+        if (lane == 0) flag_row(a, row, D3S_ROW_NONFINITE);
+      } else {
+        const int r = (rp.k + 3) >> 2;
+        float v4[4] = {pm[0], pm[1], pm[2], pm[3]};
+        const float taux = r <= 32 ? warp_tau4(v4, r, lane) : warp_rth_largest<4>(v4, rp.k);
+        const float tau = __fdiv_rn(taux, T);
+        const float rT = __frcp_rn(T);
+        const bool fast = div_rows_ok(xmin, xmax, T, gmax, tau);
+        const bool clamp = !(__fsub_rn(__fdiv_rn(xmin, T), gmax) >= kTermFloor);
+        float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                         make_float2(0.0f, 0.0f)};
+        unsigned long long bits[NBW];
+#pragma unroll
+        for (int j = 0; j < NBW; ++j) bits[j] = 0ull;
+        if (fast && !clamp)
+          rw_pass2<NC, BF16, true, false>(stage, lane, s, V, cfull, T, rT, gmax, tau, acc, bits);
+        else if (fast)
+          rw_pass2<NC, BF16, true, true>(stage, lane, s, V, cfull, T, rT, gmax, tau, acc, bits);
+        else
+          rw_pass2<NC, BF16, false, true>(stage, lane, s, V, cfull, T, rT, gmax, tau, acc, bits);
+        // the lane's eight partials, each truncated to 2^-46 fixed point, added exactly
+        unsigned long long fx = 0ull;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          fx += __float2ull_rz(__fmul_rn(acc[j].x, 0x1p46f)) + __float2ull_rz(__fmul_rn(acc[j].y, 0x1p46f));
+        const unsigned long long S = warp_sum_u64(fx);
+        lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
+        // candidates into the warp's list
+        int mine = 0;
+#pragma unroll
+        for (int j = 0; j < NBW; ++j) mine += __popcll(bits[j]);
+        int incl = mine;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int o = __shfl_up_sync(kFull, incl, d);
+          if (lane >= d) incl += o;
+        }
+        C = __shfl_sync(kFull, incl, 31);
+        if (C > kCandCap) {
+          if (lane == 0) defer_row(a, row);
+        } else {
+          int pos = incl - mine;
+#pragma unroll
+          for (int j = 0; j < NBW; ++j) {
+            unsigned long long m = bits[j];
+            while (m) {
+              const int b = 64 * j + __ffsll((long long)m) - 1;
+              m &= m - 1;
+              const int i = b / EPC, e = b - i * EPC;
+              const int p = EPC * (lane + 32 * i) + e;
+              float xv;
+              if constexpr (BF16)
+                xv = __uint_as_float((unsigned)reinterpret_cast<const unsigned short *>(stage)[p] << 16);
+              else
+                xv = reinterpret_cast<const float *>(stage)[p];
+              cs[pos++] = cand_key(__fdiv_rn(xv, T), (uint32_t)(p - s));
+            }
+          }
+          go = true;
+        }
+      }
+    }
+    // the stage has been read: start the next row's copy into it
+    __syncwarp();
+    if (lane == 0 && nrow < a.N) {
+      fence_proxy_async();
+      issue_row<ESZ>(a, nrow, stage, bar, pol);
+    }
+    if (go) {
+      const int k = rp.k;
+      if (C <= 32)
+        sort_list<1>(cs, C, k, lane);
+      else if (C <= 64)
+        sort_list<2>(cs, C, k, lane);
+      else if (C <= 128)
+        sort_list<4>(cs, C, k, lane);
+      else
+        select_list(cs, C, k, lane);
+      __syncwarp();
+      sample_tail(a, row, raw_key(a, cur), cs, scr, k, lse, rp.p, lane);
+    }
+    __syncwarp();
   }
 }
 
@@ -1112,6 +1453,49 @@ int launch_fast(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStr
   return launch_wide<BF16>(a, 1, wide_kcap, st);
 }
 
+template <bool BF16, int NC>
+int launch_rowwarp_nc(const KArgs &a, cudaStream_t st) {
+  const int stage_bytes = NC * 512;  // every chunk a lane may read
+  const size_t smem = (size_t)stage_bytes + kRwTailBytes;
+  auto fn = sample_rowwarp_kernel<NC, BF16>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+      cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    return D3S_ERR_CUDA;
+  const int sms = device_sms();
+  if (sms <= 0) return D3S_ERR_CUDA;
+  const int grid = std::max(1, std::min(a.N, sms * occupancy((const void *)fn, 32, smem)));
+  fn<<<grid, 32, smem, st>>>(a, stage_bytes);
+  return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+}
+
+// Chunks of 16 bytes a lane reads for rows of V elements (the stage starts up to
+// one chunk before the row); 0 when the row-warp kernel does not take V.
+template <bool BF16>
+int rowwarp_nc(int V) {
+  constexpr int EPC = BF16 ? 8 : 4;
+  const int chunks = (V + 2 * EPC - 2) / EPC;
+  const int nc = (chunks + 31) / 32;
+  const int opts[] = {1, 2, 3, 5, 9, 17, 25, 33};
+  for (int o : opts)
+    if (nc <= o) return o;
+  return 0;
+}
+
+template <bool BF16>
+int launch_rowwarp(const KArgs &a, int nc, cudaStream_t st) {
+  switch (nc) {
+    case 1: return launch_rowwarp_nc<BF16, 1>(a, st);
+    case 2: return launch_rowwarp_nc<BF16, 2>(a, st);
+    case 3: return launch_rowwarp_nc<BF16, 3>(a, st);
+    case 5: return launch_rowwarp_nc<BF16, 5>(a, st);
+    case 9: return launch_rowwarp_nc<BF16, 9>(a, st);
+    case 17: return launch_rowwarp_nc<BF16, 17>(a, st);
+    case 25: return launch_rowwarp_nc<BF16, 25>(a, st);
+    case 33: return launch_rowwarp_nc<BF16, 33>(a, st);
+    default: return D3S_ERR_ARG;
+  }
+}
+
 template <bool BF16>
 int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
   const bool scalar_k = a.k_rows == nullptr;
@@ -1119,8 +1503,19 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
   const int kscalar = std::min(a.top_k, a.V);
   if (J == 0 || (scalar_k && kscalar > kFastMaxK))
     return launch_wide<BF16>(a, 0, scalar_k ? kscalar : D3S_MAX_K, st);
-  if (!s.deferred || !s.counters || s.capacity < a.N || !s.heads || s.rec_capacity < a.N)
-    return D3S_ERR_ARG;
+  if (!s.deferred || !s.counters || s.capacity < a.N) return D3S_ERR_ARG;
+  // One warp per row (then the wide kernel for the rows it handed on) for short
+  // rows, where the kernel is compact and many warps fit on an SM, and for
+  // batches of at most one wave, where fewer launches matter more than issue
+  // efficiency; long rows in large batches go to the stats + select kernels
+  // (four warps share a row: more warps resident per row in flight).
+  const int nc = rowwarp_nc<BF16>(a.V);
+  if (nc > 0 && (nc <= 9 || a.N <= kRowWarpMaxBatch)) {
+    const int rc = launch_rowwarp<BF16>(a, nc, st);
+    if (rc != D3S_OK) return rc;
+    return launch_wide<BF16>(a, 1, scalar_k ? kscalar : D3S_MAX_K, st);
+  }
+  if (!s.heads || s.rec_capacity < a.N) return D3S_ERR_ARG;
   return launch_fast<BF16>(a, s, J, scalar_k ? kscalar : D3S_MAX_K, st);
 }
 

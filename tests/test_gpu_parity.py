@@ -234,6 +234,26 @@ def test_rows_config5_per_row_params(ctx, oracle, synth):
     assert ids.cpu().numpy().tolist() == want.tolist()
 
 
+@pytest.mark.parametrize("dtype,V,N", [("f32", 2049, 2500), ("f32", 6000, 2500), ("bf16", 4097, 2500),
+                                        ("f32", 4097, 2048), ("bf16", 1024, 3000)])
+def test_rows_both_kernel_paths(ctx, oracle, dtype, V, N):
+    """Large batches of long rows run the stats + select kernels, batches of at
+    most 2048 rows and short rows the one-warp-per-row kernel: both against
+    the oracle on per-row parameters."""
+    rng = np.random.default_rng(V + N)
+    x = (rng.standard_normal((N, V)) * 3.0).astype(np.float32)
+    T = rng.uniform(0.5, 1.2, N).astype(np.float32)
+    p = rng.uniform(0.5, 1.0, N).astype(np.float32)
+    k = rng.integers(1, 65, N).astype(np.int32)
+    seeds = np.arange(N, dtype=np.int64) * 3 + V
+    xt = dev(x, torch.bfloat16 if dtype == "bf16" else torch.float32)
+    ids = torch.empty(N, dtype=torch.int32, device="cuda")
+    ctx.sample_rows(xt, ids, temperature=dev(T), top_p=dev(p), top_k=dev(k), seeds=dev(seeds))
+    want = oracle.sample_rows(host_logits(xt), T, p, k, seeds.astype(np.uint64))
+    assert ids.cpu().numpy().tolist() == want.tolist()
+    ctx.check()
+
+
 def test_per_row_k_above_fast_limit_is_deferred(ctx, oracle):
     """Rows with k > 256 go through the wide kernel's hand-off list; a second
     launch checks the list counters were re-zeroed."""

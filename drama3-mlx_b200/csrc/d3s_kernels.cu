@@ -346,7 +346,7 @@ __device__ __forceinline__ int resolve(const KArgs &a, const RawP &r, RowP &rp) 
 
 // ---- stats kernel (K1): the streaming pass over the rows ----
 
-constexpr int kStatMinBlocks = 5;
+constexpr int kStatMinBlocks = 6;
 
 struct alignas(16) StatSmem {
   uint64_t mbar[kMaxStages];
@@ -421,13 +421,12 @@ __device__ __forceinline__ void sum_and_mask(const float (&q)[kFastPP][JJ], floa
 template <int JJ, bool BF16, bool EXACT>
 __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &Cs,
                                           unsigned *cand_n, const unsigned char *rb,
-                                          float (&q)[kFastPP][JJ], float T, float gmax, float tau,
-                                          float xmin, bool fast, int t, int lane, int w) {
+                                          float (&q)[kFastPP][JJ], float T, float rT, float gmax,
+                                          float tau, float xminq, bool fast, int t, int lane, int w) {
   constexpr int PP = kFastPP;
   constexpr int NT = kFastThreads;
   const int V = a.V;
   if (fast) {
-    const float rT = __frcp_rn(T);
     const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-T, -T);
 #pragma unroll
     for (int j = 0; j < JJ; ++j) {
@@ -447,7 +446,7 @@ __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &
   float2 s2 = make_float2(0.0f, 0.0f);
   unsigned long long bits = 0ull;
   // every term's d >= the row's smallest d: when that is >= -86 the floor is a no-op
-  if (__fsub_rn(__fdiv_rn(xmin, T), gmax) >= kTermFloor)
+  if (__fsub_rn(xminq, gmax) >= kTermFloor)
     sum_and_mask<JJ, false, EXACT>(q, gmax, tau, t, V, s2, bits);
   else
     sum_and_mask<JJ, true, EXACT>(q, gmax, tau, t, V, s2, bits);
@@ -470,7 +469,10 @@ __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &
     bits &= bits - 1;
     const int m = b / JJ, j = b - m * JJ;
     const int i = t + NT * m + kPartials * j;
-    const float qi = __fdiv_rn(lds_x<BF16>(rb, i), T);
+    const float xi = lds_x<BF16>(rb, i);
+    // the reciprocal path is the IEEE quotient for |x| in [2^-100, 2^60] (zero excluded:
+    // it would lose the sign of -0)
+    const float qi = fast && fabsf(xi) >= 0x1p-100f ? div_rows(xi, rT, -T) : __fdiv_rn(xi, T);
     if (pos < kCandCap) Cs.cand[pos] = cand_key(qi, (uint32_t)i);
     ++pos;
   }
@@ -602,11 +604,17 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
         xmin = fminf(xmin, sm.red_min[par][i]);
         taux = fminf(taux, sm.red_tau[par][i]);
       }
-      const float gmax = __fdiv_rn(xmax, rp.T);  // max(x / T) = RN(max(x) / T): RN is monotone
-      const float tau = __fdiv_rn(taux, rp.T);
+      // the row's four quotients in one divide across lanes: max (max(x / T) =
+      // RN(max(x) / T), RN being monotone), threshold, min, and 1 / T (= RN(1 / T))
+      const float num = lane == 0 ? xmax : (lane == 1 ? taux : (lane == 2 ? xmin : 1.0f));
+      const float quo = __fdiv_rn(num, rp.T);
+      const float gmax = __shfl_sync(kFull, quo, 0);
+      const float tau = __shfl_sync(kFull, quo, 1);
+      const float xminq = __shfl_sync(kFull, quo, 2);
+      const float rT = __shfl_sync(kFull, quo, 3);
       if (fabsf(gmax) < f_inf())
-        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q, rp.T, gmax, tau,
-                                   xmin, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);
+        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q, rp.T, rT, gmax, tau,
+                                   xminq, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);
       else if (t == 0) {  // NaN, +inf, or every value -inf
         flag_row(a, row, D3S_ROW_NONFINITE);
         H.done = 1;
@@ -830,7 +838,7 @@ __device__ __forceinline__ void stage_row(const RowHead *heads, const RowCands *
                reinterpret_cast<const char *>(cands + row) + 16 * c);
 }
 
-__global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KArgs a,
+__global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KArgs a,
                                                                         const RowHead *heads,
                                                                         const RowCands *cands) {
   __shared__ __align__(16) float scr_all[kSelWarps][kFastMaxK + 4];

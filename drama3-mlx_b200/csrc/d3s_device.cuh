@@ -242,6 +242,14 @@ __host__ __device__ __forceinline__ uint2 seed_subkey(uint64_t seed) {
   return k1;
 }
 
+// seed_subkey computed by a whole warp: lanes 0 and 1 evaluate the two
+// threefry blocks of the split side by side (every lane must call it).
+__device__ __forceinline__ uint2 seed_subkey_warp(uint64_t seed, int lane) {
+  const uint32_t c = (uint32_t)(lane & 1);
+  const uint2 r = threefry2x32(key_from_seed(seed), make_uint2(c, c + 2u));
+  return make_uint2(__shfl_sync(0xffffffffu, r.y, 0), __shfl_sync(0xffffffffu, r.y, 1));
+}
+
 // random::uniform(0, 1, float32): float(bits) / 2^32, clamped below 1.
 __device__ __forceinline__ float bits_to_uniform(uint32_t b) {
   return fminf(__fmul_rn(__uint2float_rn(b), 0x1p-32f), kUniformUpper);

@@ -327,9 +327,10 @@ __device__ __forceinline__ RawP load_raw(const KArgs &a, int row) {
   return r;
 }
 
-// The key that draws the row's uniforms, from its stored parameters.
-__device__ __forceinline__ uint2 raw_key(const KArgs &a, const RawP &r) {
-  if (a.noise == D3S_NOISE_SEEDS) return seed_subkey(r.seed);
+// The key that draws the row's uniforms, from its stored parameters (called by
+// every lane of a warp).
+__device__ __forceinline__ uint2 raw_key(const KArgs &a, const RawP &r, int lane) {
+  if (a.noise == D3S_NOISE_SEEDS) return seed_subkey_warp(r.seed, lane);
   if (a.noise == D3S_NOISE_KEYS) return make_uint2((unsigned)r.seed, (unsigned)(r.seed >> 32));
   return a.key;
 }
@@ -679,13 +680,13 @@ __device__ __forceinline__ void inreg_exchange(unsigned long long &x, unsigned l
 }
 
 // Bitonic sort of 32 * S keys held as v[s] = element lane + 32 s, descending.
-// The stage loops stay rolled (small code); only the S keys of a lane unroll.
+// Fully unrolled: every stage's direction and partner masks are constants.
 template <int S>
 __device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int lane) {
   constexpr int n = 32 * S;
-#pragma unroll 1
+#pragma unroll
   for (int size = 2; size <= n; size <<= 1) {
-#pragma unroll 1
+#pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       if (stride < 32) {
 #pragma unroll
@@ -884,7 +885,7 @@ __global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KAr
       } else {
         const RowCands &Cs = cands[row];
         const float lse = __fadd_rn(st.head.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
-        const uint2 key = raw_key(a, raw);
+        const uint2 key = raw_key(a, raw, lane);
         if (C <= 32)
           sort_cands<1>(st.cand, Cs, C, rp.k, sk, lane);
         else if (C <= 64)
@@ -1192,7 +1193,7 @@ __global__ void __launch_bounds__(32, RwBounds<NC>::kMinBlocks)
       else
         select_list(cs, C, k, lane);
       __syncwarp();
-      sample_tail(a, row, raw_key(a, cur), cs, scr, k, lse, rp.p, lane);
+      sample_tail(a, row, raw_key(a, cur, lane), cs, scr, k, lse, rp.p, lane);
     }
     __syncwarp();
   }

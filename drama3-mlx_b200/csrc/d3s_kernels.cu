@@ -391,69 +391,81 @@ __device__ __forceinline__ void defer_row(const KArgs &a, int row) {
     flag_row(a, row, D3S_ROW_BADPARAM);
 }
 
+// A candidate as the stats kernel stores it: x's bits above its id. The select
+// kernel turns it into the (value, id) key of q = x / T (IEEE divide).
+__device__ __forceinline__ unsigned long long raw_cand(float x, uint32_t id) {
+  return ((unsigned long long)__float_as_uint(x) << 32) | id;
+}
+__device__ __forceinline__ unsigned long long raw_to_key(unsigned long long r, float T) {
+  return cand_key(__fdiv_rn(__uint_as_float((uint32_t)(r >> 32)), T), (uint32_t)r);
+}
+
+// 32-bit mask of the predicate x >= y (NaN compares false): all ones or zero.
+__device__ __forceinline__ uint32_t ge_mask(float x, float y) {
+  uint32_t m;
+  asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(m) : "f"(x), "f"(y));
+  return m;
+}
+
 // The rest of a row once its max and threshold are known: q = x / T in place
 // (per-row reciprocal when the range allows, IEEE divide otherwise), the two
 // packed partial sums of exp(q - max) in fixed point, and every element >= tau
-// written as a (value, id) key into this warp's slots: a bit per element in
-// registers, one warp prefix sum, then a short loop over the set bits that
-// re-reads x from the stage and recomputes its q.
+// written as a raw (x, id) candidate into the row's list: one bit per element in two
+// 32-bit words (x: partial t, y: partial t + 128; bit j = column j), one warp
+// prefix sum, then a short loop over the set bits that re-reads x from the
+// stage. q2[j] holds elements t + 256 j (x) and
+// t + 128 + 256 j (y) as one register pair, the operand of the packed ops.
 template <int JJ, bool CLAMP, bool EXACT>
-__device__ __forceinline__ void sum_and_mask(const float (&q)[kFastPP][JJ], float gmax, float tau,
-                                             int t, int V, float2 &s2,
-                                             unsigned long long &bits) {
-  constexpr int PP = kFastPP;
+__device__ __forceinline__ void sum_and_mask(const float2 (&q2)[JJ], float gmax, float tau, int t,
+                                             int V, float2 &s2, uint32_t &bx, uint32_t &by) {
   constexpr int NT = kFastThreads;
+  static_assert(JJ <= 32, "one mask word per partial");
   const float2 mg = make_float2(-gmax, -gmax);
 #pragma unroll
   for (int j = 0; j < JJ; ++j) {
-    float2 e = exp_term2<CLAMP>(__fadd2_rn(make_float2(q[0][j], q[PP - 1][j]), mg));
+    float2 e = exp_term2<CLAMP>(__fadd2_rn(q2[j], mg));
+    uint32_t mx = ge_mask(q2[j].x, tau), my = ge_mask(q2[j].y, tau);
     if (!(EXACT && j < JJ - 1)) {  // a column that can run past V: padding adds exactly 0
-      if (t + kPartials * j >= V) e.x = 0.0f;
-      if (t + NT * (PP - 1) + kPartials * j >= V) e.y = 0.0f;
+      if (t + kPartials * j >= V) {
+        e.x = 0.0f;
+        mx = 0u;
+      }
+      if (t + NT + kPartials * j >= V) {
+        e.y = 0.0f;
+        my = 0u;
+      }
     }
     s2 = __fadd2_rn(s2, e);
-#pragma unroll
-    for (int m = 0; m < PP; ++m)
-      if (q[m][j] >= tau && ((EXACT && j < JJ - 1) || t + NT * m + kPartials * j < V))
-        bits |= 1ull << (m * JJ + j);
+    bx |= mx & (1u << j);
+    by |= my & (1u << j);
   }
 }
 
 template <int JJ, bool BF16, bool EXACT>
 __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &Cs,
                                           unsigned *cand_n, const unsigned char *rb,
-                                          float (&q)[kFastPP][JJ], float T, float rT, float gmax,
+                                          float2 (&q2)[JJ], float T, float rT, float gmax,
                                           float tau, float xminq, bool fast, int t, int lane, int w) {
-  constexpr int PP = kFastPP;
   constexpr int NT = kFastThreads;
   const int V = a.V;
   if (fast) {
     const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-T, -T);
 #pragma unroll
-    for (int j = 0; j < JJ; ++j) {
-      const float2 r2 = div_rows2(make_float2(q[0][j], q[PP - 1][j]), rT2, mT2);
-      q[0][j] = r2.x;
-      q[PP - 1][j] = r2.y;
-    }
-#pragma unroll
-    for (int m = 0; m < PP; ++m)  // padding past V stays -inf (only the last column has any)
-      if (t + NT * m + kPartials * (JJ - 1) >= V) q[m][JJ - 1] = -f_inf();
+    for (int j = 0; j < JJ; ++j) q2[j] = div_rows2(q2[j], rT2, mT2);
   } else {
 #pragma unroll
-    for (int m = 0; m < PP; ++m)
-#pragma unroll
-      for (int j = 0; j < JJ; ++j) q[m][j] = __fdiv_rn(q[m][j], T);
+    for (int j = 0; j < JJ; ++j) q2[j] = make_float2(__fdiv_rn(q2[j].x, T), __fdiv_rn(q2[j].y, T));
   }
   float2 s2 = make_float2(0.0f, 0.0f);
-  unsigned long long bits = 0ull;
+  uint32_t bx = 0u, by = 0u;
   // every term's d >= the row's smallest d: when that is >= -86 the floor is a no-op
   if (__fsub_rn(xminq, gmax) >= kTermFloor)
-    sum_and_mask<JJ, false, EXACT>(q, gmax, tau, t, V, s2, bits);
+    sum_and_mask<JJ, false, EXACT>(q2, gmax, tau, t, V, s2, bx, by);
   else
-    sum_and_mask<JJ, true, EXACT>(q, gmax, tau, t, V, s2, bits);
+    sum_and_mask<JJ, true, EXACT>(q2, gmax, tau, t, V, s2, bx, by);
   const unsigned long long wsum = warp_sum_fixed(__float2ull_rz(__fmul_rn(s2.x, 0x1p46f)) +
                                                  __float2ull_rz(__fmul_rn(s2.y, 0x1p46f)));
-  const int mine = __popcll(bits);
+  const int mine = __popc(bx) + __popc(by);
   int incl = mine;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
@@ -465,17 +477,17 @@ __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &
   if (lane == 31 && incl > 0) base = atomicAdd(cand_n, (unsigned)incl);
   base = __shfl_sync(kFull, base, 31);
   int pos = (int)base + incl - mine;
-  while (bits) {
-    const int b = __ffsll((long long)bits) - 1;
-    bits &= bits - 1;
-    const int m = b / JJ, j = b - m * JJ;
-    const int i = t + NT * m + kPartials * j;
-    const float xi = lds_x<BF16>(rb, i);
-    // the reciprocal path is the IEEE quotient for |x| in [2^-100, 2^60] (zero excluded:
-    // it would lose the sign of -0)
-    const float qi = fast && fabsf(xi) >= 0x1p-100f ? div_rows(xi, rT, -T) : __fdiv_rn(xi, T);
-    if (pos < kCandCap) Cs.cand[pos] = cand_key(qi, (uint32_t)i);
-    ++pos;
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    uint32_t bits = m ? by : bx;
+    while (bits) {
+      const int j = __ffs(bits) - 1;
+      bits &= bits - 1;
+      const int i = t + NT * m + kPartials * j;
+      // the raw candidate (x, id); the select kernel divides and keys it
+      if (pos < kCandCap) Cs.cand[pos] = raw_cand(lds_x<BF16>(rb, i), (uint32_t)i);
+      ++pos;
+    }
   }
   if (lane == 31) H.sum[w] = wsum;
   if (t == 0) {
@@ -542,21 +554,22 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
     const unsigned char *rb =
         dsm + (size_t)s * span +
         (((uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ) & 15);
-    float q[PP][JJ];
-    float pm[PP];
+    static_assert(PP == 2, "two partials per thread, one packed pair per column");
+    float2 q2[JJ];
+    float pm[PP] = {-f_inf(), -f_inf()};
     float pmn = f_inf();
 #pragma unroll
-    for (int m = 0; m < PP; ++m) {
-      pm[m] = -f_inf();
-#pragma unroll
-      for (int j = 0; j < JJ; ++j) {
-        const int i = t + NT * m + kPartials * j;
-        const bool valid = (EXACT && j < JJ - 1) || i < V;
-        const float v = valid ? lds_x<BF16>(rb, i) : -f_inf();
-        q[m][j] = v;
-        pm[m] = max_nan(pm[m], v);
-        if (valid) pmn = fminf(pmn, v);
-      }
+    for (int j = 0; j < JJ; ++j) {
+      const int i0 = t + kPartials * j, i1 = i0 + NT;
+      const bool v0 = (EXACT && j < JJ - 1) || i0 < V;
+      const bool v1 = (EXACT && j < JJ - 1) || i1 < V;
+      const float x0 = v0 ? lds_x<BF16>(rb, i0) : -f_inf();  // padding: -inf
+      const float x1 = v1 ? lds_x<BF16>(rb, i1) : -f_inf();
+      q2[j] = make_float2(x0, x1);
+      pm[0] = max_nan(pm[0], x0);
+      pm[1] = max_nan(pm[1], x1);
+      if (v0) pmn = fminf(pmn, x0);
+      if (v1) pmn = fminf(pmn, x1);
     }
     {
       const float lm = max_nan(pm[0], pm[PP - 1]);
@@ -614,7 +627,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       const float xminq = __shfl_sync(kFull, quo, 2);
       const float rT = __shfl_sync(kFull, quo, 3);
       if (fabsf(gmax) < f_inf())
-        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q, rp.T, rT, gmax, tau,
+        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q2, rp.T, rT, gmax, tau,
                                    xminq, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);
       else if (t == 0) {  // NaN, +inf, or every value -inf
         flag_row(a, row, D3S_ROW_NONFINITE);
@@ -716,12 +729,13 @@ __device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int l
 // into sk.
 template <int S>
 __device__ __forceinline__ void sort_cands(const unsigned long long *cs, const RowCands &Cs,
-                                           int C, int k, unsigned long long *sk, int lane) {
+                                           int C, int k, float T, unsigned long long *sk,
+                                           int lane) {
   unsigned long long v[S];
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     const int e = lane + 32 * s;
-    v[s] = e < C ? (e < kStageCands ? cs[e] : Cs.cand[e]) : 0ull;
+    v[s] = e < C ? raw_to_key(e < kStageCands ? cs[e] : Cs.cand[e], T) : 0ull;
   }
   warp_sort_desc<S>(v, lane);
 #pragma unroll
@@ -731,13 +745,13 @@ __device__ __forceinline__ void sort_cands(const unsigned long long *cs, const R
 
 // More than 128 candidates: the k largest taken one at a time (two warp reduxes
 // per rank), into sk in rank order.
-__device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k,
+__device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k, float T,
                                              unsigned long long *sk, int lane) {
   unsigned long long v[8], best = 0ull;
 #pragma unroll
   for (int s = 0; s < 8; ++s) {
     const int e = lane + 32 * s;
-    v[s] = e < C ? Cs.cand[e] : 0ull;
+    v[s] = e < C ? raw_to_key(Cs.cand[e], T) : 0ull;
     best = v[s] > best ? v[s] : best;
   }
   for (int r = 0; r < k; ++r) {
@@ -887,13 +901,13 @@ __global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KAr
         const float lse = __fadd_rn(st.head.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
         const uint2 key = raw_key(a, raw, lane);
         if (C <= 32)
-          sort_cands<1>(st.cand, Cs, C, rp.k, sk, lane);
+          sort_cands<1>(st.cand, Cs, C, rp.k, rp.T, sk, lane);
         else if (C <= 64)
-          sort_cands<2>(st.cand, Cs, C, rp.k, sk, lane);
+          sort_cands<2>(st.cand, Cs, C, rp.k, rp.T, sk, lane);
         else if (C <= 128)
-          sort_cands<4>(st.cand, Cs, C, rp.k, sk, lane);
+          sort_cands<4>(st.cand, Cs, C, rp.k, rp.T, sk, lane);
         else
-          select_cands(Cs, C, rp.k, sk, lane);
+          select_cands(Cs, C, rp.k, rp.T, sk, lane);
         __syncwarp();
         sample_tail(a, row, key, sk, scr_all[w], rp.k, lse, rp.p, lane);
       }

@@ -45,8 +45,9 @@ struct KArgs {
 
 // Per-row results the stats kernel passes to the select kernel. The header
 // (dense, one per row): the row max in q, the candidate count and the four
-// warps' 2^-46 fixed-point partial sums. The candidates, as (value, id) keys in
-// no particular order, live in a separate slab.
+// warps' 2^-46 fixed-point partial sums. The candidates, as raw (x bits, id)
+// pairs in no particular order (the select kernel divides and keys them), live
+// in a separate slab.
 struct alignas(16) RowHead {
   float gmax;
   int done;  // 1: the stats kernel already wrote the row's result (or handed it on)

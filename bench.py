@@ -259,6 +259,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import d3s
+    import shard
     import synth
     rank, world, local = env_ranks()
     torch.cuda.set_device(local)
@@ -270,15 +271,14 @@ def run_ours(args):
     ctx.reserve(rows)
     x, T, p, k, seeds = synth.c5_batch(rows, seed=1000 + rank)
     ids = torch.empty(rows, dtype=torch.int32, device="cuda")
-    gather = [torch.empty_like(ids) for _ in range(world)] if (world > 1 and rank == 0) else None
     st = torch.cuda.current_stream()
 
     def sample():
         ctx.sample_rows(x, ids, temperature=T, top_p=p, top_k=k, seeds=seeds)
 
-    def collect():
+    def collect():  # the sampled ids of every rank to rank 0 (drama3-mlx_b200/shard.py)
         if world > 1:
-            dist.gather(ids, gather, dst=0)
+            shard.gather_ids(ids, world * rows, world, rank)
 
     def barrier():
         if world > 1:
@@ -336,7 +336,7 @@ def run_ours(args):
             ctx.sample_rows(dx, did, temperature=dT, top_p=dp, top_k=dk, seeds=ds)
             hids.copy_(did, non_blocking=True)
             if world > 1:
-                dist.gather(did, gather, dst=0)
+                shard.gather_ids(did, world * rows, world, rank)
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):

@@ -41,7 +41,7 @@ EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split"
            "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
            "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3s_sample_rows_static",
            "d3_sample", "d3s_last_status", "d3s_keys_next", "d3s_frame_main", "d3s_lmhead",
-           "d3s_lmhead_sample")
+           "d3s_lmhead_sample", "d3s_codes_write_npy")
 RAS_WINDOW = 16
 FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
 STATIC_MAX_ROWS = 4096
@@ -135,6 +135,7 @@ def lib() -> ctypes.CDLL:
         L.d3s_keys_next.argtypes = [vp, vp, i32, i32, vp, i64, vp]
         L.d3s_frame_main.argtypes = [vp, ctypes.POINTER(FrameRequest), vp]
         L.d3s_lmhead.argtypes = [vp, vp, i64, vp, i64, i32, i32, i32, vp, i64, vp]
+        L.d3s_codes_write_npy.argtypes = [ctypes.c_char_p, vp, i32, i32, i32]
         L.d3s_lmhead_sample.argtypes = [vp, vp, i64, vp, i64, i32, ctypes.POINTER(Request), vp]
         _lib = L
     return _lib
@@ -168,6 +169,15 @@ def next_key(state: Key | None = None) -> Key:
     sub = Key()
     _check(lib().d3s_next_key(ctypes.byref(state) if state is not None else None, ctypes.byref(sub)))
     return sub
+
+
+def codes_write_npy(path, frames, n_codebooks: int) -> None:
+    """Write the codes of a take (frames: int32 array [n_frames, 1 + n_codebooks
+    or wider], column 0 the main token) as the reference's codes .npy."""
+    import numpy as np
+    fr = np.ascontiguousarray(frames, dtype=np.int32)
+    _check(lib().d3s_codes_write_npy(str(path).encode(), fr.ctypes.data, fr.shape[0], fr.shape[1],
+                                     n_codebooks))
 
 
 def sample_rows_static(logits, ids, temperature, top_p, top_k, seeds, stream=None) -> None:

@@ -231,6 +231,15 @@ typedef struct {
  * keys = sub + 2 + j, ld_keys = n. */
 D3S_API int d3s_frame_main(d3s_ctx *ctx, const d3s_frame_request *req, void *stream);
 
+/* Host: the codes of a take as a .npy file, as npy_write_codes writes them
+ * (src/npy.c:98-129, src/generate.c:162-168). frames is [n_frames, width]
+ * int32 host memory, one sampled frame row per decode step (column 0 the main
+ * token, columns 1..n_codebooks the codes: c0 then the heads); the file holds
+ * codes[k][t] = frames[t][1 + k] as little-endian int64, shape
+ * (n_codebooks, n_frames). */
+D3S_API int d3s_codes_write_npy(const char *path, const int32_t *frames, int n_frames, int width,
+                                int n_codebooks);
+
 /* ---- the lm_head projection in front of the sampler ---- */
 
 /* backbone_audio_logits -> m_linear (src/backbone.c:1213, src/mlxu.c:442-496):

@@ -98,3 +98,29 @@ def test_lmhead_rejects_bad_arguments(ctx):
     with pytest.raises(d3s.D3SError):
         ctx.lmhead(torch.zeros(4, 12, dtype=torch.bfloat16, device="cuda"),
                    torch.zeros(9, 12, dtype=torch.bfloat16, device="cuda"))  # D % 8
+
+
+@pytest.mark.parametrize("D", [1024, 2048])
+def test_tower_head_projection_and_draw(ctx, oracle, D):
+    """A codebook head of a frame: m_linear(out, heads[j]) (src/tower.c:264,
+    :313) for 512 streams, W [1024, D], then the head draw with each stream's
+    own subkey (column 2 + j of the frame's key table), in one call."""
+    import d3s
+    S, V, j = 512, 1024, 3
+    g = torch.Generator(device="cuda").manual_seed(D)
+    h = torch.randn(S, D, generator=g, device="cuda").to(torch.bfloat16)
+    W = (torch.randn(V, D, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    rng = np.random.default_rng(D)
+    table = rng.integers(0, 2**32, (S, 11, 2), dtype=np.uint64).astype(np.uint32)
+    tdev = torch.from_numpy(table.view(np.int32)).cuda()
+    logits = torch.empty(S, V, dtype=torch.bfloat16, device="cuda")
+    ids = torch.empty(S, dtype=torch.int32, device="cuda")
+    ctx.lmhead_sample(h, W, logits, ids, temperature=1.0, top_p=0.9, top_k=30,
+                      noise=d3s.NOISE_KEYS, keys=tdev[:, 2 + j])
+    torch.cuda.synchronize()
+    ctx.check()
+    check_logits(logits, h, W)
+    import synth
+    want = oracle.sample_rows_keys(synth.to_host_logits(logits), 1.0, 0.9, 30,
+                                   np.ascontiguousarray(table[:, 2 + j:]))
+    np.testing.assert_array_equal(ids.cpu().numpy(), want)

@@ -233,40 +233,48 @@ __device__ __forceinline__ float warp_rth_largest(float (&v)[M], int r) {
 __device__ __forceinline__ void sample_tail(const KArgs &a, int row, uint2 key,
                                          const unsigned long long *sorted, float *scr, int k,
                                          float lse, float top_p, int lane) {
-  for (int r = lane; r < k; r += 32) scr[r] = exp_full(__fsub_rn(cand_value(sorted[r]), lse));
+  // e_r = exp(v_r - lse), zero past k up to the next multiple of 4 (adding +0
+  // leaves every running sum unchanged)
+  const int k4 = (k + 3) & ~3;
+  float lsum = 0.0f;
+  for (int r = lane; r < k4; r += 32) {
+    const float e = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lse)) : 0.0f;
+    scr[r] = e;
+    lsum = __fadd_rn(lsum, e);
+  }
+  // Any-order sum of the k terms: a sequential sum of nonnegative terms differs
+  // from it by at most 2 (k - 1) 2^-24 relative (< 3.1e-5 for k <= 256). When
+  // even that bound stays <= top_p, no prefix sum can exceed top_p: nothing is cut.
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lsum = __fadd_rn(lsum, __shfl_xor_sync(kFull, lsum, o));
   __syncwarp();
   int kept = k;
-  {
+  if (!(__fmul_rn(lsum, 1.0001f) <= top_p)) {
+    // cum_r = e_0 + ... + e_r in rank order; the first r > 0 with cum_r > top_p
+    // is the cut. Four ranks per step: the running sums, then one test.
     float cum = 0.0f;
     for (int r0 = 0; r0 < k; r0 += 4) {
       const float4 e4 = *reinterpret_cast<const float4 *>(scr + r0);
-      const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-      bool stop = false;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = r0 + i;
-        if (!stop && r < k) {
-          cum = __fadd_rn(cum, ev[i]);
-          if (r > 0 && cum > top_p) {
-            kept = r;
-            stop = true;
-          }
-        }
+      const float c0 = __fadd_rn(cum, e4.x), c1 = __fadd_rn(c0, e4.y);
+      const float c2 = __fadd_rn(c1, e4.z), c3 = __fadd_rn(c2, e4.w);
+      const bool h0 = r0 > 0 && c0 > top_p;  // rank 0 is never dropped
+      if (h0 || c1 > top_p || c2 > top_p || c3 > top_p) {
+        kept = h0 ? r0 : (c1 > top_p ? r0 + 1 : (c2 > top_p ? r0 + 2 : r0 + 3));
+        break;
       }
-      if (stop) break;
+      cum = c3;
     }
   }
   __syncwarp();
   const float top = cand_value(sorted[0]);
-  for (int r = lane; r < kept; r += 32) scr[r] = exp_full(__fsub_rn(cand_value(sorted[r]), top));
+  const int kept4 = (kept + 3) & ~3;
+  for (int r = lane; r < kept4; r += 32)
+    scr[r] = r < kept ? exp_full(__fsub_rn(cand_value(sorted[r]), top)) : 0.0f;
   __syncwarp();
   float sum = 0.0f;
   for (int r0 = 0; r0 < kept; r0 += 4) {
     const float4 e4 = *reinterpret_cast<const float4 *>(scr + r0);
-    const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (r0 + i < kept) sum = __fadd_rn(sum, ev[i]);
+    sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, e4.x), e4.y), e4.z), e4.w);
   }
   const float inv = __fdiv_rn(1.0f, sum);
   float best = -1.0f;

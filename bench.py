@@ -440,8 +440,18 @@ def run_c3(args):
     ids = torch.empty(B, dtype=torch.int32, device="cuda")
     seeds = torch.arange(B, dtype=torch.int64, device="cuda")
     # the weight (16.8 MB) fits in L2: flush between projection launches so each one
-    # reads W from HBM, as a decode step that ran the backbone in between would
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    # reads W from HBM, as a decode step that ran the backbone in between would. The
+    # flush READS 256 MB (a sum), leaving clean lines: a written buffer would leave
+    # dirty lines whose write-back competes with the projection's reads.
+    flush_buf = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    flush_out = torch.empty((), dtype=torch.float32, device="cuda")
+
+    class _Flush:
+        @staticmethod
+        def zero_():
+            torch.sum(flush_buf, dim=0, out=flush_out)
+
+    flush = _Flush()
     st = torch.cuda.current_stream()
 
     def proj():
@@ -487,7 +497,7 @@ def run_c3(args):
         "higher_is_better": True, "dtype": "bf16 x bf16 -> f32 accumulate -> bf16 logits",
         "data": "synthetic", "config": {"workload": f"config3: h bf16 [{B}, {D}] ~N(0,1), W bf16 [{V}, {D}] "
                                         "~N(0,0.02), T 0.7, top_p 0.7, top_k 30, per-row seeds",
-                                        "l2": "256 MB buffer written between launches"},
+                                        "l2": "256 MB buffer read between launches"},
         "projection_ms": proj_ms,
         "projection_kernel": "lmhead_gemv_kernel" if B <= 8 else "lmhead_gemm_kernel (tcgen05)",
         "roofline": ({"bound": "tensor", "achieved": tfs, "peak": peak_tf, "unit": "TFLOP/s",

@@ -24,6 +24,8 @@ struct d3s_ctx {
   size_t rows_cap = 0;
   cudaStream_t stream = nullptr;
   d3s::FrameScratch frame;  // d3s_frame_main's per-draw arrays
+  float *lm_ws = nullptr;   // d3s_lmhead's split-K partials
+  int64_t lm_ws_cap = 0;    // floats
 };
 
 namespace {
@@ -319,6 +321,7 @@ void d3s_ctx_destroy(d3s_ctx *ctx) {
   cudaFree(ctx->ids_dev);
   cudaFree(ctx->status_dev);
   cudaFree(ctx->frame.keys);
+  cudaFree(ctx->lm_ws);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -534,6 +537,20 @@ int d3s_lmhead(d3s_ctx *ctx, const void *h_dev, int64_t ld_h, const void *W_dev,
   a.out = logits_dev;
   a.ld_out = ld_logits;
   a.error = reinterpret_cast<int32_t *>(ctx->scratch.counters + 2);
+  const int64_t need = d3s::lmhead_workspace(B, V, D);
+  if (need > ctx->lm_ws_cap) {
+    float *w = nullptr;
+    const cudaError_t e = cudaMalloc(&w, (size_t)need * sizeof(float));
+    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "lm_head workspace: %s", cudaGetErrorString(e));
+    if (ctx->lm_ws) {
+      cudaDeviceSynchronize();  // queued projections may still use the old one
+      cudaFree(ctx->lm_ws);
+    }
+    ctx->lm_ws = w;
+    ctx->lm_ws_cap = need;
+  }
+  a.ws = ctx->lm_ws;
+  a.ws_cap = ctx->lm_ws_cap;
   rc = d3s::launch_lmhead(a, (cudaStream_t)stream);
   if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "lm_head launch");
   return D3S_OK;

@@ -22,6 +22,9 @@
 // from global memory (L2) in each pass, selection by exact bisection on the
 // 64-bit (value, id) key, bitonic sort of the k winners in shared memory.
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "d3s_device.cuh"
 #include "d3s_kernels.cuh"
@@ -521,7 +524,22 @@ __device__ __forceinline__ float warp_rth_of32(float v, int r, int lane) {
 // candidate threshold, one barrier; then stats_row; the last warp to finish
 // with a stage refills it with the row `stages` ahead.
 // EXACT: JJ == ceil(V / 256), so only the last column can run past V.
-template <int JJ, bool BF16, bool EXACT>
+// Declared here, defined with the select kernel.
+template <int S>
+__device__ __forceinline__ void sort_cands(const unsigned long long *cs, const RowCands &Cs,
+                                           int C, int k, float T, unsigned long long *sk,
+                                           int lane);
+__device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k, float T,
+                                             unsigned long long *sk, int lane);
+
+// The select kernel's work on one row whose record is complete: the row's
+// lse, its subkey, the top k of its candidates in rank order in sk, the tail.
+__device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHead &H,
+                                           const unsigned long long *cs, const RowCands &Cs,
+                                           const RawP &raw, const RowP &rp,
+                                           unsigned long long *sk, float *scr, int lane);
+
+template <int JJ, bool BF16, bool EXACT, bool SELECT>
 __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
     sample_stats_kernel(const KArgs a, RowHead *heads, RowCands *cands, int stages, int span) {
   extern __shared__ __align__(128) unsigned char dsm[];
@@ -663,6 +681,16 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
           issue_row<ESZ>(a, nrow, dsm + (size_t)s * span, &sm.mbar[s], pol);
         }
       }
+    }
+    if constexpr (SELECT) {
+      // One row per CTA (small batches): once every warp has added its
+      // candidates, warp 0 samples the row; the stage is free and holds the
+      // sorted keys and the tail's scratch.
+      __syncthreads();
+      if (w == 0 && !H.done)
+        select_row(a, row, H, cands[row].cand, cands[row], cur, rp,
+                   reinterpret_cast<unsigned long long *>(dsm),
+                   reinterpret_cast<float *>(dsm + kCandCap * 8), lane);
     }
   }
   if (failed) {
@@ -861,6 +889,32 @@ __device__ __forceinline__ void stage_row(const RowHead *heads, const RowCands *
                reinterpret_cast<const char *>(cands + row) + 16 * c);
 }
 
+__device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHead &H,
+                                           const unsigned long long *cs, const RowCands &Cs,
+                                           const RawP &raw, const RowP &rp,
+                                           unsigned long long *sk, float *scr, int lane) {
+  const int C = H.cnt;
+  unsigned long long S = 0;
+#pragma unroll
+  for (int i = 0; i < kFastW; ++i) S += H.sum[i];
+  if (C > kCandCap) {  // more candidates than the list holds (ties): the wide kernel's exact path
+    if (lane == 0) defer_row(a, row);
+    return;
+  }
+  const float lse = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
+  const uint2 key = raw_key(a, raw, lane);
+  if (C <= 32)
+    sort_cands<1>(cs, Cs, C, rp.k, rp.T, sk, lane);
+  else if (C <= 64)
+    sort_cands<2>(cs, Cs, C, rp.k, rp.T, sk, lane);
+  else if (C <= 128)
+    sort_cands<4>(cs, Cs, C, rp.k, rp.T, sk, lane);
+  else
+    select_cands(Cs, C, rp.k, rp.T, sk, lane);
+  __syncwarp();
+  sample_tail(a, row, key, sk, scr, rp.k, lse, rp.p, lane);
+}
+
 __global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KArgs a,
                                                                         const RowHead *heads,
                                                                         const RowCands *cands) {
@@ -898,27 +952,7 @@ __global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KAr
     if (!st.head.done) {
       RowP rp;
       resolve(a, raw, rp);  // valid: the stats kernel flagged every other row
-      const int C = st.head.cnt;
-      unsigned long long S = 0;
-#pragma unroll
-      for (int i = 0; i < kFastW; ++i) S += st.head.sum[i];
-      if (C > kCandCap) {  // more candidates than the list holds (ties): the wide kernel's exact path
-        if (lane == 0) defer_row(a, row);
-      } else {
-        const RowCands &Cs = cands[row];
-        const float lse = __fadd_rn(st.head.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
-        const uint2 key = raw_key(a, raw, lane);
-        if (C <= 32)
-          sort_cands<1>(st.cand, Cs, C, rp.k, rp.T, sk, lane);
-        else if (C <= 64)
-          sort_cands<2>(st.cand, Cs, C, rp.k, rp.T, sk, lane);
-        else if (C <= 128)
-          sort_cands<4>(st.cand, Cs, C, rp.k, rp.T, sk, lane);
-        else
-          select_cands(Cs, C, rp.k, rp.T, sk, lane);
-        __syncwarp();
-        sample_tail(a, row, key, sk, scr_all[w], rp.k, lse, rp.p, lane);
-      }
+      select_row(a, row, st.head, st.cand, cands[row], raw, rp, sk, scr_all[w], lane);
     }
     raw = rawn;
     cnt_next = cnt_nn;
@@ -950,6 +984,7 @@ constexpr int kRwCandBytes = kCandCap * 8;
 constexpr int kRwScrBytes = (kFastMaxK + 4) * 4;
 constexpr int kRwTailBytes = kRwCandBytes + kRwScrBytes + 16;  // + the mbarrier
 constexpr int kRowWarpMaxBatch = 2048;  // long rows: batches up to this take the row-warp kernel
+constexpr int kSmallBatch = 512;        // batches up to this: one CTA per row, select in the same launch
 
 // min over four 32-lane columns (v[c] of every lane) of each column's r-th
 // largest value (1 <= r <= 32): four interleaved bitonic sorts.
@@ -1388,26 +1423,26 @@ __global__ void div_check_kernel(const float *Ts, int nT, uint64_t lo, uint64_t 
 
 using StatFn = void (*)(const KArgs, RowHead *, RowCands *, int, int);
 
-template <bool BF16, bool EXACT>
+template <bool BF16, bool EXACT, bool SELECT>
 StatFn pick_stats_e(int J) {
   switch (J) {
-    case 1: return sample_stats_kernel<1, BF16, EXACT>;
-    case 2: return sample_stats_kernel<2, BF16, EXACT>;
-    case 4: return sample_stats_kernel<4, BF16, EXACT>;
-    case 8: return sample_stats_kernel<8, BF16, EXACT>;
-    case 12: return sample_stats_kernel<12, BF16, EXACT>;
-    case 16: return sample_stats_kernel<16, BF16, EXACT>;
-    case 17: return sample_stats_kernel<17, BF16, EXACT>;
-    case 24: return sample_stats_kernel<24, BF16, EXACT>;
-    case 32: return sample_stats_kernel<32, BF16, EXACT>;
+    case 1: return sample_stats_kernel<1, BF16, EXACT, SELECT>;
+    case 2: return sample_stats_kernel<2, BF16, EXACT, SELECT>;
+    case 4: return sample_stats_kernel<4, BF16, EXACT, SELECT>;
+    case 8: return sample_stats_kernel<8, BF16, EXACT, SELECT>;
+    case 12: return sample_stats_kernel<12, BF16, EXACT, SELECT>;
+    case 16: return sample_stats_kernel<16, BF16, EXACT, SELECT>;
+    case 17: return sample_stats_kernel<17, BF16, EXACT, SELECT>;
+    case 24: return sample_stats_kernel<24, BF16, EXACT, SELECT>;
+    case 32: return sample_stats_kernel<32, BF16, EXACT, SELECT>;
     default: return nullptr;
   }
 }
 
-template <bool BF16>
+template <bool BF16, bool SELECT>
 StatFn pick_stats(int J, int V) {
-  return J == (V + kPartials - 1) / kPartials ? pick_stats_e<BF16, true>(J)
-                                              : pick_stats_e<BF16, false>(J);
+  return J == (V + kPartials - 1) / kPartials ? pick_stats_e<BF16, true, SELECT>(J)
+                                              : pick_stats_e<BF16, false, SELECT>(J);
 }
 
 int pick_J(int V) {
@@ -1438,6 +1473,36 @@ int occupancy(const void *fn, int threads, size_t smem) {
   return std::max(blocks, 1);
 }
 
+// Per device and kernel: raise the dynamic shared-memory limit once (and, when
+// asked, the largest shared-memory carveout), and remember the occupancy per (threads, smem).
+// The attribute calls and the occupancy query cost microseconds each, more
+// than a one-row launch takes on the GPU. Returns blocks per SM, or 0 when an
+// attribute call failed.
+int prepare(const void *fn, int threads, size_t smem, bool max_carveout = false) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void *>, size_t> limit;
+  static std::map<std::tuple<int, const void *, int, size_t>, int> occ;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(dev, fn);
+  auto it = limit.find(key);
+  if (it == limit.end() || it->second < smem) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return 0;
+    if (max_carveout && it == limit.end() &&
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return 0;
+    limit[key] = smem;
+  }
+  const auto ok = std::make_tuple(dev, fn, threads, smem);
+  auto jt = occ.find(ok);
+  if (jt != occ.end()) return jt->second;
+  const int b = occupancy(fn, threads, smem);
+  occ[ok] = b;
+  return b;
+}
+
 size_t wide_smem(int kcap) {
   int kp = 2;
   while (kp < kcap) kp <<= 1;
@@ -1445,15 +1510,15 @@ size_t wide_smem(int kcap) {
 }
 
 template <bool BF16>
-int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st) {
+int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st, int max_grid = 1 << 30) {
   const size_t smem = wide_smem(kcap);
   auto fn = sample_wide_kernel<BF16>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
-    return D3S_ERR_CUDA;
+  const int occ = prepare((const void *)fn, kWideThreads, smem);
+  if (occ <= 0) return D3S_ERR_CUDA;
   const int sms = device_sms();
-  int grid = sms * occupancy((const void *)fn, kWideThreads, smem);
+  int grid = sms * occ;
   if (!use_list) grid = std::min(grid, a.N);
+  grid = std::min(grid, max_grid);
   if (grid < 1) grid = 1;
   fn<<<grid, kWideThreads, smem, st>>>(a, use_list, kcap);
   return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
@@ -1467,21 +1532,35 @@ int launch_fast(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStr
   int stages = BF16 ? 3 : 2;
   while (stages > 2 && (size_t)stages * span > 64 * 1024) --stages;
   const size_t smem = (size_t)stages * span;
-  StatFn fn = pick_stats<BF16>(J, a.V);
+  StatFn fn = pick_stats<BF16, false>(J, a.V);
   if (!fn) return D3S_ERR_ARG;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
-    return D3S_ERR_CUDA;
+  const int occ = prepare((const void *)fn, kFastThreads, smem);
   const int sms = device_sms();
-  if (sms <= 0) return D3S_ERR_CUDA;
-  const int grid = std::max(1, std::min(a.N, sms * occupancy((const void *)fn, kFastThreads, smem)));
+  if (occ <= 0 || sms <= 0) return D3S_ERR_CUDA;
+  const int grid = std::max(1, std::min(a.N, sms * occ));
   fn<<<grid, kFastThreads, smem, st>>>(a, sc.heads, sc.cands, stages, span);
   if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
-  const int sel_occ = occupancy((const void *)sample_select_kernel, kSelThreads, 0);
+  const int sel_occ = prepare((const void *)sample_select_kernel, kSelThreads, 0);
   const int sel_grid = std::max(1, std::min((a.N + kSelWarps - 1) / kSelWarps, sms * sel_occ));
   sample_select_kernel<<<sel_grid, kSelThreads, 0, st>>>(a, sc.heads, sc.cands);
   if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
   return launch_wide<BF16>(a, 1, wide_kcap, st);
+}
+
+// Small batches: one CTA per row runs the stats kernel's four warps and then,
+// in the same launch, the select work on warp 0; the wide kernel after it
+// (on at most N CTAs) takes any row handed on.
+template <bool BF16>
+int launch_small(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStream_t st) {
+  constexpr int esz = BF16 ? 2 : 4;
+  const int span = ((a.V * esz + 15) / 16) * 16 + 16;
+  const size_t smem = std::max<size_t>((size_t)span, (size_t)kCandCap * 8 + (kFastMaxK + 4) * 4);
+  StatFn fn = pick_stats<BF16, true>(J, a.V);
+  if (!fn) return D3S_ERR_ARG;
+  if (prepare((const void *)fn, kFastThreads, smem) <= 0) return D3S_ERR_CUDA;
+  fn<<<a.N, kFastThreads, smem, st>>>(a, sc.heads, sc.cands, 1, span);
+  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  return launch_wide<BF16>(a, 1, wide_kcap, st, a.N);
 }
 
 template <bool BF16, int NC>
@@ -1489,12 +1568,10 @@ int launch_rowwarp_nc(const KArgs &a, cudaStream_t st) {
   const int stage_bytes = NC * 512;  // every chunk a lane may read
   const size_t smem = (size_t)stage_bytes + kRwTailBytes;
   auto fn = sample_rowwarp_kernel<NC, BF16>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-      cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
-    return D3S_ERR_CUDA;
+  const int occ = prepare((const void *)fn, 32, smem, true);
   const int sms = device_sms();
-  if (sms <= 0) return D3S_ERR_CUDA;
-  const int grid = std::max(1, std::min(a.N, sms * occupancy((const void *)fn, 32, smem)));
+  if (occ <= 0 || sms <= 0) return D3S_ERR_CUDA;
+  const int grid = std::max(1, std::min(a.N, sms * occ));
   fn<<<grid, 32, smem, st>>>(a, stage_bytes);
   return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
 }
@@ -1540,6 +1617,9 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
   // batches of at most one wave, where fewer launches matter more than issue
   // efficiency; long rows in large batches go to the stats + select kernels
   // (four warps share a row: more warps resident per row in flight).
+  const int kcap = scalar_k ? kscalar : D3S_MAX_K;
+  if (a.N <= kSmallBatch && s.heads && s.rec_capacity >= a.N)
+    return launch_small<BF16>(a, s, J, kcap, st);
   const int nc = rowwarp_nc<BF16>(a.V);
   if (nc > 0 && (nc <= 9 || a.N <= kRowWarpMaxBatch)) {
     const int rc = launch_rowwarp<BF16>(a, nc, st);
@@ -1551,6 +1631,8 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
 }
 
 }  // namespace
+
+int prepare_launch(const void *fn, int threads, size_t smem) { return prepare(fn, threads, smem); }
 
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t st) {
   if (a.N == 0) return D3S_OK;

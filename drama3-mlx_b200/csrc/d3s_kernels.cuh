@@ -72,6 +72,10 @@ struct Scratch {
   int64_t rec_capacity = 0;
 };
 
+// Raise fn's dynamic shared-memory limit to smem once per device and return its
+// blocks per SM for (threads, smem), cached; 0 when an attribute call failed.
+int prepare_launch(const void *fn, int threads, size_t smem);
+
 // Launch the sampler for one request. Validates sizes; returns D3S_* status.
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t stream);
 
@@ -110,8 +114,12 @@ struct LmArgs {
   void *out;
   int64_t ld_out;
   int32_t *error;  // bit 1 set when a bounded wait in the GEMM gave up
+  float *ws;       // split-K partials (device), lmhead_workspace() floats
+  int64_t ws_cap;
 };
 int launch_lmhead(const LmArgs &a, cudaStream_t stream);
+// fp32 workspace floats launch_lmhead needs for (B, V, D) on the current device
+int64_t lmhead_workspace(int B, int V, int D);
 
 // Advance S key states by n splits each; subkeys at sub[s * ld_sub + i].
 int launch_keys_next(uint2 *state, int S, int n, uint2 *sub, int64_t ld_sub, cudaStream_t stream);

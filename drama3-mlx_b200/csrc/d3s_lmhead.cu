@@ -155,7 +155,8 @@ template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     lmhead_gemm_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmH, __nv_bfloat16 *out,
-                       int64_t ld_out, int V, int B, int KT, int32_t *error) {
+                       int64_t ld_out, int V, int B, int KT, int kps, float *ws,
+                       int32_t *error) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ unsigned char dsmem[];
@@ -169,6 +170,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kBM;  // first W row (logit id) of the tile
   const int n0 = blockIdx.y * BN;   // first batch row of the tile
+  // split K: this CTA's k-tiles [kt0, kt0 + nk); its partial goes to ws
+  const int kt0 = blockIdx.z * kps;
+  const int nk = min(KT - kt0, kps);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -194,13 +198,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     // producer: W tile [128 x 64] and h tile [BN x 64] per stage
     int issued = 0;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % S;
-      if (kt >= S && !bar_wait(&empty[s], ((kt / S) & 1) ^ 1, abort_flag)) break;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      if (i >= S && !bar_wait(&empty[s], ((i / S) & 1) ^ 1, abort_flag)) break;
       unsigned char *st = base + (size_t)s * Cfg::kStageBytes;
       bar_expect_tx(&full[s], Cfg::kStageBytes);
-      tma_load_2d(st, &tmW, kt * kBK, m0, &full[s]);
-      tma_load_2d(st + Cfg::kABytes, &tmH, kt * kBK, n0, &full[s]);
+      tma_load_2d(st, &tmW, (kt0 + i) * kBK, m0, &full[s]);
+      tma_load_2d(st + Cfg::kABytes, &tmH, (kt0 + i) * kBK, n0, &full[s]);
       ++issued;
     }
     if (*abort_flag) {  // let the copies still in flight land before the CTA exits
@@ -213,16 +217,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // MMA issuer
     constexpr uint32_t idesc = umma_idesc(kBM, BN);
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % S;
-      if (!bar_wait(&full[s], (kt / S) & 1, abort_flag)) break;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      if (!bar_wait(&full[s], (i / S) & 1, abort_flag)) break;
       tc_fence_after();
       const uint32_t a0 = saddr(base + (size_t)s * Cfg::kStageBytes);
       const uint32_t b0 = a0 + Cfg::kABytes;
 #pragma unroll
       for (int kk = 0; kk < kBK / kUK; ++kk)
         umma_bf16(tmem, sw128_desc(a0 + kk * kUK * 2), sw128_desc(b0 + kk * kUK * 2), idesc,
-                  (kt | kk) != 0 ? 1u : 0u);
+                  (i | kk) != 0 ? 1u : 0u);
       umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
     }
     umma_commit(accum);  // arrives when every MMA issued above is complete
@@ -237,10 +241,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
       if (ok && !*abort_flag && v < V) {
+        if (ws) {  // split K: the fp32 partial of this CTA's k-tiles
+          float *wz = ws + (size_t)blockIdx.z * B * V;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int b = n0 + c + j;
-          if (b < B) out[(int64_t)b * ld_out + v] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          for (int j = 0; j < 32; ++j) {
+            const int b = n0 + c + j;
+            if (b < B) wz[(size_t)b * V + v] = __uint_as_float(r[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int b = n0 + c + j;
+            if (b < B) out[(int64_t)b * ld_out + v] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
         }
       }
     }
@@ -254,6 +267,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                  : "memory");
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(error, 2);
+}
+
+// Split-K sum: out[b, v] = bf16(ws[0][b][v] + ws[1][b][v] + ...), in split order.
+__global__ void lmhead_reduce_kernel(const float *ws, int KS, int B, int V, __nv_bfloat16 *out,
+                                     int64_t ld_out) {
+  const size_t n = (size_t)B * V, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float acc = ws[i];
+    for (int z = 1; z < KS; ++z) acc = __fadd_rn(acc, ws[(size_t)z * n + i]);
+    const size_t b = i / (size_t)V, v = i - b * (size_t)V;
+    out[(int64_t)b * ld_out + (int64_t)v] = __float2bfloat16_rn(acc);
+  }
 }
 
 // ---- GEMV (B <= kGemvMaxB) ----
@@ -390,19 +415,48 @@ bool make_map(CUtensorMap *m, const void *ptr, int rows, int cols, int64_t ld, i
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+int gemm_bn(int B) { return B <= 32 ? 32 : (B <= 64 ? 64 : (B <= 128 ? 128 : 256)); }
+
+// Split K when the output tiles leave most SMs idle (small B): about one CTA
+// per SM, at least four k-tiles per split.
+void gemm_splits(int B, int V, int D, int BN, int &kps, int &KS) {
+  const int KT = (D + kBK - 1) / kBK;
+  const int tiles = ((V + kBM - 1) / kBM) * ((B + BN - 1) / BN);
+  int want = std::max(1, std::min(8, sm_count() / std::max(tiles, 1)));
+  want = std::min(want, std::max(1, KT / 4));
+  kps = (KT + want - 1) / want;
+  KS = (KT + kps - 1) / kps;
+}
+
 template <int BN>
 int launch_gemm(const LmArgs &a, cudaStream_t st) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap tw, th;
   if (!make_map(&tw, a.W, a.V, a.D, a.ld_w, kBM) || !make_map(&th, a.h, a.B, a.D, a.ld_h, BN))
     return D3S_ERR_CUDA;
-  if (cudaFuncSetAttribute(lmhead_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)Cfg::kSmem) != cudaSuccess)
+  if (prepare_launch((const void *)lmhead_gemm_kernel<BN>, kGemmThreads, Cfg::kSmem) <= 0)
     return D3S_ERR_CUDA;
-  const dim3 grid((a.V + kBM - 1) / kBM, (a.B + BN - 1) / BN);
   const int KT = (a.D + kBK - 1) / kBK;
+  int kps = KT, KS = 1;
+  gemm_splits(a.B, a.V, a.D, BN, kps, KS);
+  if (KS > 1 && (!a.ws || a.ws_cap < (int64_t)KS * a.B * a.V)) return D3S_ERR_ARG;
+  const dim3 grid((a.V + kBM - 1) / kBM, (a.B + BN - 1) / BN, KS);
+  __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(a.out);
   lmhead_gemm_kernel<BN><<<grid, kGemmThreads, Cfg::kSmem, st>>>(
-      tw, th, reinterpret_cast<__nv_bfloat16 *>(a.out), a.ld_out, a.V, a.B, KT, a.error);
+      tw, th, out, a.ld_out, a.V, a.B, KT, kps, KS > 1 ? a.ws : nullptr, a.error);
+  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  if (KS > 1) {
+    const size_t n = (size_t)a.B * a.V;
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+    lmhead_reduce_kernel<<<blocks, 256, 0, st>>>(a.ws, KS, a.B, a.V, out, a.ld_out);
+  }
   return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
 }
 
@@ -426,6 +480,13 @@ int launch_gemv(const LmArgs &a, cudaStream_t st) {
 }
 
 }  // namespace
+
+int64_t lmhead_workspace(int B, int V, int D) {
+  if (B <= kGemvMaxB) return 0;
+  int kps, KS;
+  gemm_splits(B, V, D, gemm_bn(B), kps, KS);
+  return KS > 1 ? (int64_t)KS * B * V : 0;
+}
 
 int launch_lmhead(const LmArgs &a, cudaStream_t st) {
   if (a.B == 0 || a.V == 0) return D3S_OK;

@@ -195,7 +195,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
+    if (lane == 0) {
     // producer: W tile [128 x 64] and h tile [BN x 64] per stage
     int issued = 0;
     for (int i = 0; i < nk; ++i) {
@@ -214,7 +215,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
-  } else if (warp == 1 && lane == 0) {
+    }
+    __syncwarp();  // the warp reconverges before the CTA barrier
+  } else if (warp == 1) {
+    if (lane == 0) {
     // MMA issuer
     constexpr uint32_t idesc = umma_idesc(kBM, BN);
     for (int i = 0; i < nk; ++i) {
@@ -230,6 +234,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
     }
     umma_commit(accum);  // arrives when every MMA issued above is complete
+    }
+    __syncwarp();
   } else if (warp >= 2) {
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = W rows of the tile
     const int q = warp & 3;
@@ -279,6 +285,179 @@ __global__ void lmhead_reduce_kernel(const float *ws, int KS, int B, int V, __nv
     const size_t b = i / (size_t)V, v = i - b * (size_t)V;
     out[(int64_t)b * ld_out + (int64_t)v] = __float2bfloat16_rn(acc);
   }
+}
+
+// ---- 2-SM GEMM (B >= 256): a CTA pair shares one 256 x 256 UMMA tile ----
+//
+// tcgen05.mma.cta_group::2 with M = 256 (W rows), N = 256 (batch rows): each
+// CTA of the pair stages its 128 W rows and its 128 batch rows per K step
+// (32 KB; the pair's MMA reads both CTAs' stages) and holds its 128 output rows
+// x 256 columns in its own TMEM. Per K step a CTA moves 32 KB for the work a
+// single-CTA 128 x 256 tile moves 48 KB for, so six stages hide the L2
+// latency. The leader (rank 0) issues the MMAs; both CTAs' loads complete on
+// the leader's full barrier (mapa address); the leader commits each stage to
+// its own and to its peer's empty barrier, and the result to both accumulator
+// barriers (two plain commits: no multicast anywhere).
+
+constexpr int kStages2 = 6;
+constexpr int kPairMinB = 512;  // from here the pair tiles alone fill the GPU (V = 4097: 136 CTAs at B = 1024)
+constexpr uint32_t kHalfBytes = 128 * kBK * 2;        // 128 rows x 64 k of bf16
+constexpr uint32_t kStageBytes2 = 2 * kHalfBytes;     // this CTA's W half + h half
+constexpr size_t kSmem2 = (size_t)kStages2 * kStageBytes2 + (2 * kStages2 + 1) * 8 + 16 + 1024;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// shared::cluster address of the same object in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *tm, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(saddr(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void umma2_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrives on the mbarrier at a shared::cluster address once the issued MMAs complete
+__device__ __forceinline__ void umma2_commit(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
+}
+
+constexpr int kGemm2Threads = 320;  // warp 0: TMA, warp 1: TMEM + MMA, warps 2-9: epilogue
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
+    lmhead_gemm2_kernel(const __grid_constant__ CUtensorMap tmW,
+                        const __grid_constant__ CUtensorMap tmH, __nv_bfloat16 *out,
+                        int64_t ld_out, int V, int B, int KT, int32_t *error) {
+  constexpr int S = kStages2;
+  extern __shared__ unsigned char dsmem[];
+  unsigned char *base = (unsigned char *)(((uintptr_t)dsmem + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + (size_t)S * kStageBytes2);
+  uint64_t *empty = full + S;
+  uint64_t *accum = empty + S;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank(), peer = rank ^ 1u;
+  const bool leader = rank == 0;
+  const int m0 = blockIdx.x * kBM;                       // this CTA's 128 W rows
+  const int n0 = blockIdx.y * 256;                       // the pair's 256 batch rows
+  const int nh = n0 + (int)rank * 128;                   // this CTA's half of them
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    bar_init(accum, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(256)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before any load or commit targets them
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+    const uint32_t full0 = peer_addr(&full[0], 0);  // the leader's full barriers
+    int issued = 0;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % S;
+      if (kt >= S && !bar_wait(&empty[s], ((kt / S) & 1) ^ 1, abort_flag)) break;
+      unsigned char *st = base + (size_t)s * kStageBytes2;
+      if (leader) bar_expect_tx(&full[s], 2 * kStageBytes2);  // both CTAs' halves
+      tma_load_2d_pair(st, &tmW, kt * kBK, m0, full0 + 8 * s);
+      tma_load_2d_pair(st + kHalfBytes, &tmH, kt * kBK, nh, full0 + 8 * s);
+      ++issued;
+    }
+    if (*abort_flag && leader) {  // let the pair's copies in flight land before exiting
+      for (int kt = issued - S > 0 ? issued - S : 0; kt < issued; ++kt) {
+        const unsigned long long t0 = now_ns();
+        while (!bar_try(&full[kt % S], (kt / S) & 1) && now_ns() - t0 < kLmWaitLimitNs) {
+        }
+      }
+    }
+    }
+    __syncwarp();  // the warp reconverges before the CTA barrier
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+    constexpr uint32_t idesc = umma_idesc(2 * kBM, 256);
+    const uint32_t empty_peer = peer_addr(&empty[0], peer), accum_peer = peer_addr(accum, peer);
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % S;
+      if (!bar_wait(&full[s], (kt / S) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t a0 = saddr(base + (size_t)s * kStageBytes2);
+      const uint32_t b0 = a0 + kHalfBytes;
+#pragma unroll
+      for (int kk = 0; kk < kBK / kUK; ++kk)
+        umma2_bf16(tmem, sw128_desc(a0 + kk * kUK * 2), sw128_desc(b0 + kk * kUK * 2), idesc,
+                   (kt | kk) != 0 ? 1u : 0u);
+      umma2_commit(saddr(&empty[s]));  // the stage is free in both CTAs once these MMAs are done
+      umma2_commit(empty_peer + 8 * s);
+    }
+    umma2_commit(saddr(accum));
+    umma2_commit(accum_peer);
+    }
+    __syncwarp();
+  } else {
+    // epilogue, warps 2..9: warp w reads TMEM lanes 32 (w % 4) .. + 31 (this CTA's
+    // W rows) and columns [128 h, 128 h + 128), h = (w - 2) / 4
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const bool ok = bar_wait(accum, 0, abort_flag);
+    tc_fence_after();
+    const int v = m0 + q * 32 + lane;
+    const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(128 * h);
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) {
+      uint32_t r[32];
+      tmem_ld32(ta + 32 * i, r);
+      if (ok && !*abort_flag && v < V) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int b = n0 + 128 * h + 32 * i + j;
+          if (b < B) out[(int64_t)b * ld_out + v] = __float2bfloat16_rn(__uint_as_float(r[j]));
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_sync_all();  // the pair's MMAs, loads and reads are over before TMEM and smem go away
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256)
+                 : "memory");
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(error, 2);
 }
 
 // ---- GEMV (B <= kGemvMaxB) ----
@@ -460,6 +639,20 @@ int launch_gemm(const LmArgs &a, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
 }
 
+int launch_gemm2(const LmArgs &a, cudaStream_t st) {
+  CUtensorMap tw, th;
+  if (!make_map(&tw, a.W, a.V, a.D, a.ld_w, kBM) || !make_map(&th, a.h, a.B, a.D, a.ld_h, 128))
+    return D3S_ERR_CUDA;
+  if (prepare_launch((const void *)lmhead_gemm2_kernel, kGemm2Threads, kSmem2) <= 0)
+    return D3S_ERR_CUDA;
+  const int mt = (a.V + kBM - 1) / kBM;
+  const dim3 grid((mt + 1) & ~1, (a.B + 255) / 256);  // whole CTA pairs along W rows
+  const int KT = (a.D + kBK - 1) / kBK;
+  lmhead_gemm2_kernel<<<grid, kGemm2Threads, kSmem2, st>>>(
+      tw, th, reinterpret_cast<__nv_bfloat16 *>(a.out), a.ld_out, a.V, a.B, KT, a.error);
+  return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+}
+
 template <int NB>
 int launch_gemv(const LmArgs &a, cudaStream_t st) {
   const size_t smem = (size_t)NB * a.D * 2;
@@ -482,7 +675,7 @@ int launch_gemv(const LmArgs &a, cudaStream_t st) {
 }  // namespace
 
 int64_t lmhead_workspace(int B, int V, int D) {
-  if (B <= kGemvMaxB) return 0;
+  if (B <= kGemvMaxB || B >= kPairMinB) return 0;
   int kps, KS;
   gemm_splits(B, V, D, gemm_bn(B), kps, KS);
   return KS > 1 ? (int64_t)KS * B * V : 0;
@@ -497,7 +690,8 @@ int launch_lmhead(const LmArgs &a, cudaStream_t st) {
   if (a.B <= 32) return launch_gemm<32>(a, st);
   if (a.B <= 64) return launch_gemm<64>(a, st);
   if (a.B <= 128) return launch_gemm<128>(a, st);
-  return launch_gemm<256>(a, st);
+  if (a.B < kPairMinB) return launch_gemm<256>(a, st);
+  return launch_gemm2(a, st);
 }
 
 }  // namespace d3s

@@ -38,7 +38,8 @@ def check_logits(out, h, W):
     assert same >= 0.99, same
 
 
-@pytest.mark.parametrize("B", [1, 2, 3, 4, 5, 8, 9, 16, 33, 64, 100, 128, 200, 256, 1024])
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 5, 8, 9, 16, 33, 64, 100, 128, 200, 256, 511, 512, 600,
+                               1024])
 def test_projection_c3(ctx, B):
     import synth
     h, W = synth.c3_inputs(B, seed=B)
@@ -49,7 +50,7 @@ def test_projection_c3(ctx, B):
 
 
 @pytest.mark.parametrize("B,V,D", [(1, 1024, 256), (7, 300, 64), (64, 1024, 1024), (40, 4097, 2056),
-                                   (300, 129, 512)])
+                                   (300, 129, 512), (777, 300, 256), (600, 4097, 2056), (512, 1, 64)])
 def test_projection_shapes(ctx, B, V, D):
     g = torch.Generator(device="cuda").manual_seed(B * 7 + V)
     h = torch.randn(B, D, generator=g, device="cuda").to(torch.bfloat16)

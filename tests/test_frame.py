@@ -305,3 +305,56 @@ def test_c4_frames_end_to_end(ctx, oracle):
                 u = oracle.uniform(o_subs[s, 2 + j], 30)
                 assert codes[2 + j][s] == oracle.sample_row(heads[j, s], 0.8, 0.9, 30, u)[0]
     np.testing.assert_array_equal(_keys_host(st_dev), o_state)
+
+
+@pytest.mark.gpu
+def test_frame_step_replays_from_a_cuda_graph(ctx, oracle):
+    """One decode frame (key advance, main + retry, 9 head draws) captured once in
+    a CUDA graph and replayed frame after frame gives the same codes as the same
+    calls made one by one (scratch reserved and every kernel prepared before the
+    capture, so nothing in the step allocates or queries the device)."""
+    rng = np.random.default_rng(12)
+    S, Vb, Vh, H = 64, 1 + VOCAB, 1024, 9
+    xb = torch.from_numpy(_frame_logits(S, Vb, rng)[0]).to(torch.bfloat16).cuda()
+    heads = torch.from_numpy((rng.standard_normal((H, S, Vh)) * 2.5).astype(np.float32)).to(
+        torch.bfloat16).cuda()
+    st0 = rng.integers(0, 2**32, (S, 2), dtype=np.uint64).astype(np.uint32)
+    ctx.reserve(2 * S)
+
+    def make_state():
+        return (_keys_dev(st0), torch.zeros(S, 16, dtype=torch.int32, device="cuda"),
+                torch.zeros(S, dtype=torch.int32, device="cuda"),
+                torch.empty(S, 2 + H, 2, dtype=torch.int32, device="cuda"),
+                torch.empty(H + 2, S, dtype=torch.int32, device="cuda"))
+
+    def step(state, stream=None):
+        states, hist, hl, sub, codes = state
+        ctx.keys_next(states, 2 + H, sub=sub, stream=stream)
+        m, c, _ = ctx.frame_main(xb, sub, hist, hl, temperature=0.8, top_p=0.9, top_k=30,
+                                 semantic_start=SEM0, code_vocab=VOCAB, eos_id=EOS, stream=stream)
+        codes[0].copy_(m)
+        codes[1].copy_(c)
+        for j in range(H):
+            ctx.sample_rows_keys(heads[j], codes[2 + j], sub[:, 2 + j], temperature=0.8,
+                                 top_p=0.9, top_k=30, stream=stream)
+
+    eager, graphed = make_state(), make_state()
+    step(make_state())  # warm-up: scratch, frame arrays and kernel attributes exist
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            step(graphed, stream=s)
+    torch.cuda.synchronize()
+    # the capture ran nothing: replay from the initial state
+    graphed[0].copy_(_keys_dev(st0))
+    graphed[1].zero_()
+    graphed[2].zero_()
+    for frame in range(3):
+        step(eager)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(eager[4], graphed[4]), frame
+        assert torch.equal(eager[0], graphed[0]) and torch.equal(eager[1], graphed[1])

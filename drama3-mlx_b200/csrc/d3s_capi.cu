@@ -26,6 +26,8 @@ struct d3s_ctx {
   d3s::FrameScratch frame;  // d3s_frame_main's per-draw arrays
   float *lm_ws = nullptr;   // d3s_lmhead's split-K partials
   int64_t lm_ws_cap = 0;    // floats
+  void *pinned = nullptr;   // d3_sample's host staging: logits, ids + status, error word
+  size_t pinned_cap = 0;    // bytes
 };
 
 namespace {
@@ -318,8 +320,8 @@ void d3s_ctx_destroy(d3s_ctx *ctx) {
   cudaFree(ctx->scratch.heads);
   cudaFree(ctx->scratch.cands);
   cudaFree(ctx->h_logits_dev);
-  cudaFree(ctx->ids_dev);
-  cudaFree(ctx->status_dev);
+  cudaFree(ctx->ids_dev);  // status_dev lives in the same allocation
+  cudaFreeHost(ctx->pinned);
   cudaFree(ctx->frame.keys);
   cudaFree(ctx->lm_ws);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -608,18 +610,32 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
   }
   if ((size_t)N > ctx->rows_cap) {
     cudaFree(ctx->ids_dev);
-    cudaFree(ctx->status_dev);
     ctx->ids_dev = nullptr;
     ctx->status_dev = nullptr;
     ctx->rows_cap = 0;
-    e = cudaMalloc(&ctx->ids_dev, (size_t)N * sizeof(int32_t));
-    if (e == cudaSuccess) e = cudaMalloc(&ctx->status_dev, (size_t)N * sizeof(int32_t));
+    // ids then status in one allocation: one copy brings both back
+    e = cudaMalloc(&ctx->ids_dev, 2 * (size_t)N * sizeof(int32_t));
     if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "ids staging: %s", cudaGetErrorString(e));
+    ctx->status_dev = ctx->ids_dev + N;
     ctx->rows_cap = (size_t)N;
   }
+  // pinned host staging: the logits, then ids + status, then the error word
+  const size_t pin = nl * sizeof(float) + 2 * (size_t)ctx->rows_cap * sizeof(int32_t) + 16;
+  if (pin > ctx->pinned_cap) {
+    cudaFreeHost(ctx->pinned);
+    ctx->pinned = nullptr;
+    ctx->pinned_cap = 0;
+    e = cudaMallocHost(&ctx->pinned, pin);
+    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "host staging: %s", cudaGetErrorString(e));
+    ctx->pinned_cap = pin;
+  }
   if (N == 0) return D3S_OK;
+  float *h_logits = static_cast<float *>(ctx->pinned);
+  int32_t *h_ids = reinterpret_cast<int32_t *>(h_logits + nl);
+  int32_t *h_err = h_ids + 2 * N;
   d3s_seed(nullptr, seed);  // m_seed(seed), src/testapi.c:159
-  e = cudaMemcpyAsync(ctx->h_logits_dev, logits, nl * sizeof(float), cudaMemcpyHostToDevice,
+  std::memcpy(h_logits, logits, nl * sizeof(float));
+  e = cudaMemcpyAsync(ctx->h_logits_dev, h_logits, nl * sizeof(float), cudaMemcpyHostToDevice,
                       ctx->stream);
   if (e != cudaSuccess) return cuda_fail(e, "logits upload");
   d3s_request r{};
@@ -641,22 +657,22 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
   r.key = sub;
   rc = d3s_sample(ctx, &r, ctx->stream);
   if (rc != D3S_OK) return rc;
-  int32_t *status = new int32_t[N];
-  e = cudaMemcpyAsync(out, ctx->ids_dev, (size_t)N * sizeof(int32_t), cudaMemcpyDeviceToHost,
+  // ids and status (adjacent on the device), then the context's error word
+  e = cudaMemcpyAsync(h_ids, ctx->ids_dev, 2 * (size_t)N * sizeof(int32_t), cudaMemcpyDeviceToHost,
                       ctx->stream);
   if (e == cudaSuccess)
-    e = cudaMemcpyAsync(status, ctx->status_dev, (size_t)N * sizeof(int32_t),
-                        cudaMemcpyDeviceToHost, ctx->stream);
+    e = cudaMemcpyAsync(h_err, ctx->scratch.counters + 2, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                        ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-  if (e != cudaSuccess) {
-    delete[] status;
-    return cuda_fail(e, "d3_sample");
-  }
+  if (e != cudaSuccess) return cuda_fail(e, "d3_sample");
+  std::memcpy(out, h_ids, (size_t)N * sizeof(int32_t));
   int bad = 0;
-  for (int i = 0; i < N; i++) bad += status[i] != D3S_ROW_OK;
-  delete[] status;
-  rc = d3s_ctx_check(ctx);
-  if (rc != D3S_OK) return rc;
+  for (int i = 0; i < N; i++) bad += h_ids[N + i] != D3S_ROW_OK;
+  if (*h_err) {
+    cudaMemsetAsync(ctx->scratch.counters + 2, 0, sizeof(uint32_t), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+    return fail(D3S_ERR_CUDA, "a sampler kernel gave up waiting for a row copy (rows left unsampled)");
+  }
   if (bad) return fail(D3S_ERR_NONFINITE, "%d row(s) had non-finite logits", bad);
   return D3S_OK;
 }

@@ -403,7 +403,7 @@ int d3s_sample_top_k_top_p(d3s_ctx *ctx, const void *logits_dev, int dtype, int 
 
 int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
                    float param, void *stream) {
-  if (!ctx || op < 0 || op > 3 || n < 0) return fail(D3S_ERR_ARG, "bad math args");
+  if (!ctx || op < 0 || op > 4 || n < 0) return fail(D3S_ERR_ARG, "bad math args");
   DeviceGuard g(ctx->device);
   const int rc = d3s::launch_math(op, x_dev, y_dev, n, param, (cudaStream_t)stream);
   if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "math launch");

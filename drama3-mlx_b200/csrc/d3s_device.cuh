@@ -90,6 +90,17 @@ __device__ __forceinline__ float scale_pow2(float p, float t) {
   return __uint_as_float(r);
 }
 
+// 2^x by the special-function unit (ex2.approx.ftz.f32): relative error below
+// 2^-22.7 wherever the result is normal (the tests measure it over every input
+// in [-127, 2^-8]), subnormal results flushed to zero. It only feeds the
+// approximate full-row sum, whose error bound the sampler carries into the
+// top-p cut (a cut it cannot certify is recomputed with the exact sum).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // One term of the full-row sum for d = q - max in [-inf, 0] (never NaN):
 // exp(max(d, -86)). Below -86 a term (< 2^-124) is far under the 2^-46
 // resolution of the fixed-point sum; the floor keeps n >= -124, so the result

@@ -224,8 +224,8 @@ __device__ __forceinline__ float warp_rth_largest(float (&v)[M], int r) {
 }
 
 // The serial end of a row, run by one warp: sorted[k] holds the top-k keys in
-// rank order, scr (>= k + 4 floats, 16-byte aligned) is scratch, key draws the
-// row's uniforms. Inclusive cumsum of exp(v - lse) in rank order
+// rank order, scr (>= 2 k + 8 floats, 16-byte aligned) is scratch, key draws
+// the row's uniforms. Inclusive cumsum of exp(v - lse) in rank order
 // (src/sampling.c:39, :126-127), drop when cum > top_p at rank > 0 (:40-43,
 // :128), softmax over the survivors with a 1/sum multiply (:44, :129-134), race
 // p / -log(1 - u) where the first strictly greater score wins (:45-47,
@@ -233,21 +233,40 @@ __device__ __forceinline__ float warp_rth_largest(float (&v)[M], int r) {
 // reads, four ranks per load). Survivors are a prefix of the ranks and every
 // survivor's score is positive unless its noise is -0, so the dropped ranks
 // (p = 0, score 0 or NaN) are drawn only when no survivor scored above 0.
-__device__ __forceinline__ void sample_tail(const KArgs &a, int row, uint2 key,
-                                         const unsigned long long *sorted, float *scr, int k,
-                                         float lse, float top_p, int lane) {
+//
+// lse is known to lie in [lse_lo, lse_hi] (equal bounds: lse is exact). With
+// an interval, the cut is found with lse_hi and then certified for every lse in
+// it: terms under a smaller lse are larger (exp's relative error, below
+// 2^-23.6, bounds how far a rounded exp can break that order), so the cut rank
+// must still pass top_p under lse_hi less a rounding margin, and the rank before
+// it must stay at or below top_p under lse_lo plus that margin. Returns false,
+// having written nothing, when the cut cannot be certified; the caller then
+// computes the exact lse and calls again.
+__device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
+                                            const unsigned long long *sorted, float *scr, int k,
+                                            float lse_lo, float lse_hi, float top_p, int lane) {
+  const bool exact = __float_as_uint(lse_lo) == __float_as_uint(lse_hi);
   // e_r = exp(v_r - lse), zero past k up to the next multiple of 4 (adding +0
-  // leaves every running sum unchanged)
+  // leaves every running sum unchanged); under an interval, scr holds the terms
+  // under lse_hi and scr_lo those under lse_lo
   const int k4 = (k + 3) & ~3;
+  float *scr_lo = exact ? scr : scr + k4;
   float lsum = 0.0f;
   for (int r = lane; r < k4; r += 32) {
-    const float e = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lse)) : 0.0f;
+    float e = 0.0f, el = 0.0f;
+    if (r < k) {
+      const float v = cand_value(sorted[r]);
+      e = exp_full(__fsub_rn(v, lse_hi));
+      el = exact ? e : exp_full(__fsub_rn(v, lse_lo));
+    }
     scr[r] = e;
-    lsum = __fadd_rn(lsum, e);
+    if (!exact) scr_lo[r] = el;
+    lsum = __fadd_rn(lsum, el);
   }
   // Any-order sum of the k terms: a sequential sum of nonnegative terms differs
   // from it by at most 2 (k - 1) 2^-24 relative (< 3.1e-5 for k <= 256). When
   // even that bound stays <= top_p, no prefix sum can exceed top_p: nothing is cut.
+  // (Under an interval the sum is of the terms under lse_lo, the largest.)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) lsum = __fadd_rn(lsum, __shfl_xor_sync(kFull, lsum, o));
   __syncwarp();
@@ -255,17 +274,33 @@ __device__ __forceinline__ void sample_tail(const KArgs &a, int row, uint2 key,
   if (!(__fmul_rn(lsum, 1.0001f) <= top_p)) {
     // cum_r = e_0 + ... + e_r in rank order; the first r > 0 with cum_r > top_p
     // is the cut. Four ranks per step: the running sums, then one test.
-    float cum = 0.0f;
+    // Under an interval the same running sums of the terms under lse_lo go
+    // alongside: before_lo is the sum of ranks 0 .. kept - 1 under lse_lo.
+    float cum = 0.0f, cut = 0.0f, cum_lo = 0.0f, before_lo = 0.0f;
     for (int r0 = 0; r0 < k; r0 += 4) {
       const float4 e4 = *reinterpret_cast<const float4 *>(scr + r0);
+      const float4 l4 = *reinterpret_cast<const float4 *>(scr_lo + r0);
       const float c0 = __fadd_rn(cum, e4.x), c1 = __fadd_rn(c0, e4.y);
       const float c2 = __fadd_rn(c1, e4.z), c3 = __fadd_rn(c2, e4.w);
+      const float l0 = __fadd_rn(cum_lo, l4.x), l1 = __fadd_rn(l0, l4.y);
+      const float l2 = __fadd_rn(l1, l4.z), l3 = __fadd_rn(l2, l4.w);
       const bool h0 = r0 > 0 && c0 > top_p;  // rank 0 is never dropped
       if (h0 || c1 > top_p || c2 > top_p || c3 > top_p) {
         kept = h0 ? r0 : (c1 > top_p ? r0 + 1 : (c2 > top_p ? r0 + 2 : r0 + 3));
+        cut = h0 ? c0 : (c1 > top_p ? c1 : (c2 > top_p ? c2 : c3));
+        before_lo = h0 ? cum_lo : (c1 > top_p ? l0 : (c2 > top_p ? l1 : l2));
         break;
       }
       cum = c3;
+      cum_lo = l3;
+    }
+    if (!exact) {
+      // margin: two sequential sums of <= kept + 1 terms (kept 2^-24 each),
+      // exp's order error (2.9 2^-24 for its error below 2^-23.5) and the
+      // product's rounding
+      const float mu = __fmul_rn((float)(2 * kept + 6), 0x1p-24f);
+      if (kept < k && !(__fmul_rn(cut, 1.0f - mu) > top_p)) return false;
+      if (kept >= 2 && !(__fmul_rn(kept < k ? before_lo : cum_lo, 1.0f + mu) <= top_p)) return false;
     }
   }
   __syncwarp();
@@ -314,6 +349,60 @@ __device__ __forceinline__ void sample_tail(const KArgs &a, int row, uint2 key,
     if (a.status) a.status[row] = D3S_ROW_OK;
     if (a.kept) a.kept[row] = kept;
   }
+  return true;
+}
+
+// Sum over the warp of each lane's fixed-point total (< 2^55): three 21/21/22-bit
+// pieces, each summed exactly by a 32-bit redux.
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+  const unsigned p0 = __reduce_add_sync(kFull, (unsigned)(v & 0x1FFFFFu));
+  const unsigned p1 = __reduce_add_sync(kFull, (unsigned)((v >> 21) & 0x1FFFFFu));
+  const unsigned p2 = __reduce_add_sync(kFull, (unsigned)(v >> 42));
+  return (unsigned long long)p0 + ((unsigned long long)p1 << 21) + ((unsigned long long)p2 << 42);
+}
+
+// The exact full-row sum of a finite row, by one warp, read back from global
+// memory: partial p (lane p % 32 holds it) is the sequential float sum of
+// exp(max(x_i / T - gmax, -86)) over i = p, p + 256, ..., truncated to 2^-46
+// fixed point; the partials are added exactly (the oracle's definition).
+// Only rows whose approximate sum left the top-p cut uncertain come here.
+__device__ __forceinline__ unsigned long long exact_row_sum(const KArgs &a, int row, float T,
+                                                         float gmax, int lane) {
+  const int V = a.V;
+  const int64_t off = phys_row(a, row) * a.ld;
+  const bool bf16 = a.dtype == D3S_BF16;
+  unsigned long long fx = 0ull;
+  for (int p = lane; p < kPartials && p < V; p += 32) {
+    float s = 0.0f;
+    for (int i = p; i < V; i += kPartials) {
+      const float x = bf16 ? load_x<true>(a.logits, off + i) : load_x<false>(a.logits, off + i);
+      s = __fadd_rn(s, exp_term(__fsub_rn(__fdiv_rn(x, T), gmax)));
+    }
+    fx += __float2ull_rz(__fmul_rn(s, 0x1p46f));
+  }
+  return warp_sum_u64(fx);
+}
+
+// Bounds on the exact lse of a row from its approximate full-row sum S (2^-46
+// fixed point, the SFU's exp2 of RN(x c + g) with c = RN(log2(e) / T) and
+// g = RN(-xmax c)).
+// With G = |max x / T| and V <= 8192, first-order error analysis bounds
+// |S_exact - S| / S by 2^-24 (3 G + 5 ln V + n_p + L + 1) + e_exp + e_ex2:
+// the quotients' and differences' roundings (2G + 2 ln V for the exact sum,
+// G + 3 ln V for the approximate one, ln V bounding the entropy-weighted |x/T -
+// max|), sequential sums of n_p <= 32 and L <= 32 terms, exp's relative error
+// (below 2^-23.5) and ex2.approx's (below 2^-22.5; both checked by the tests).
+// Rounded up: 2^-24 (3.1 G + 128). The
+// exact lse = RN(gmax + log(RN(S_exact) 2^-46)) is then bracketed by the same
+// expression at the bracket's ends: RN and log are monotone there (log is
+// checked over every float in [1, 16384) by the tests).
+__device__ __forceinline__ void lse_bounds(unsigned long long S, float gmax, float &lse_lo,
+                                           float &lse_hi) {
+  const float delta = __fmaf_ru(0x1.8cccccp-23f, fabsf(gmax), 0x1p-17f);
+  const float lo = __fmul_rd(__fmul_rd(__ull2float_rd(S), __fsub_rd(1.0f, delta)), 0x1p-46f);
+  const float hi = __fmul_ru(__fmul_ru(__ull2float_ru(S), __fadd_ru(1.0f, delta)), 0x1p-46f);
+  lse_lo = __fadd_rn(gmax, log_full(fmaxf(lo, 1.0f)));  // the exact S is at least 2^46
+  lse_hi = __fadd_rn(gmax, log_full(hi));
 }
 
 // Per-row parameters as stored (read one row ahead of use).
@@ -452,28 +541,16 @@ __device__ __forceinline__ void sum_and_mask(const float2 (&q2)[JJ], float gmax,
   }
 }
 
-template <int JJ, bool BF16, bool EXACT>
-__device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &Cs,
-                                          unsigned *cand_n, const unsigned char *rb,
-                                          float2 (&q2)[JJ], float T, float rT, float gmax,
-                                          float tau, float xminq, bool fast, int t, int lane, int w) {
+// The end of a row's stats once its sums and candidate bits are known: the
+// warp's fixed-point sum into the header, the candidates (every set bit j of bx
+// / by: element t + 256 j / t + 128 + 256 j) as raw (x, id) pairs into the
+// row's list at positions from one warp scan and one shared atomic per warp.
+template <bool BF16>
+__device__ __forceinline__ void stats_finish(RowHead &H, RowCands &Cs, unsigned *cand_n,
+                                             const unsigned char *rb, float2 s2, uint32_t bx,
+                                             uint32_t by, float gmax, int approx, int t, int lane,
+                                             int w) {
   constexpr int NT = kFastThreads;
-  const int V = a.V;
-  if (fast) {
-    const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-T, -T);
-#pragma unroll
-    for (int j = 0; j < JJ; ++j) q2[j] = div_rows2(q2[j], rT2, mT2);
-  } else {
-#pragma unroll
-    for (int j = 0; j < JJ; ++j) q2[j] = make_float2(__fdiv_rn(q2[j].x, T), __fdiv_rn(q2[j].y, T));
-  }
-  float2 s2 = make_float2(0.0f, 0.0f);
-  uint32_t bx = 0u, by = 0u;
-  // every term's d >= the row's smallest d: when that is >= -86 the floor is a no-op
-  if (__fsub_rn(xminq, gmax) >= kTermFloor)
-    sum_and_mask<JJ, false, EXACT>(q2, gmax, tau, t, V, s2, bx, by);
-  else
-    sum_and_mask<JJ, true, EXACT>(q2, gmax, tau, t, V, s2, bx, by);
   const unsigned long long wsum = warp_sum_fixed(__float2ull_rz(__fmul_rn(s2.x, 0x1p46f)) +
                                                  __float2ull_rz(__fmul_rn(s2.y, 0x1p46f)));
   const int mine = __popc(bx) + __popc(by);
@@ -504,7 +581,69 @@ __device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &
   if (t == 0) {
     H.gmax = gmax;
     H.done = 0;
+    H.approx = approx;
   }
+}
+
+template <int JJ, bool BF16, bool EXACT>
+__device__ __forceinline__ void stats_row(const KArgs &a, RowHead &H, RowCands &Cs,
+                                          unsigned *cand_n, const unsigned char *rb,
+                                          float2 (&q2)[JJ], float T, float rT, float gmax,
+                                          float tau, float xminq, bool fast, int t, int lane, int w) {
+  const int V = a.V;
+  if (fast) {
+    const float2 rT2 = make_float2(rT, rT), mT2 = make_float2(-T, -T);
+#pragma unroll
+    for (int j = 0; j < JJ; ++j) q2[j] = div_rows2(q2[j], rT2, mT2);
+  } else {
+#pragma unroll
+    for (int j = 0; j < JJ; ++j) q2[j] = make_float2(__fdiv_rn(q2[j].x, T), __fdiv_rn(q2[j].y, T));
+  }
+  float2 s2 = make_float2(0.0f, 0.0f);
+  uint32_t bx = 0u, by = 0u;
+  // every term's d >= the row's smallest d: when that is >= -86 the floor is a no-op
+  if (__fsub_rn(xminq, gmax) >= kTermFloor)
+    sum_and_mask<JJ, false, EXACT>(q2, gmax, tau, t, V, s2, bx, by);
+  else
+    sum_and_mask<JJ, true, EXACT>(q2, gmax, tau, t, V, s2, bx, by);
+  stats_finish<BF16>(H, Cs, cand_n, rb, s2, bx, by, gmax, 0, t, lane, w);
+}
+
+// The approximate row stats: each term 2^(x c + g) by the SFU (c = RN(log2(e)
+// / T), g = RN(-xmax c)), no division, no floor; candidates are the x above
+// tau_lo, a threshold just under the x-domain threshold, low enough that no x
+// at or below it can have a quotient reaching RN(taux / T) (so every element of
+// the top k is a candidate: the select step divides and keys them exactly).
+// The candidate bit of column j is the sign of tau_lo - x, shifted in from
+// the highest column down. Padding (-inf) adds +0 and sets no bit.
+template <int JJ, bool BF16>
+__device__ __forceinline__ void stats_row_approx(RowHead &H, RowCands &Cs, unsigned *cand_n,
+                                                 const unsigned char *rb, const float2 (&x2)[JJ],
+                                                 float c, float g, float tau_lo, float gmax,
+                                                 int t, int lane, int w) {
+  const float2 c2 = make_float2(c, c), g2 = make_float2(g, g);
+  const float2 tl2 = make_float2(tau_lo, tau_lo), m1 = make_float2(-1.0f, -1.0f);
+  float2 s2 = make_float2(0.0f, 0.0f);
+  uint32_t bx = 0u, by = 0u;
+#pragma unroll
+  for (int j = JJ - 1; j >= 0; --j) {
+    const float2 u = __ffma2_rn(x2[j], c2, g2);
+    s2 = __fadd2_rn(s2, make_float2(ex2_approx(u.x), ex2_approx(u.y)));
+    const float2 d = __ffma2_rn(x2[j], m1, tl2);
+    bx = __funnelshift_l(__float_as_uint(d.x), bx, 1);
+    by = __funnelshift_l(__float_as_uint(d.y), by, 1);
+  }
+  stats_finish<BF16>(H, Cs, cand_n, rb, s2, bx, by, gmax, 1, t, lane, w);
+}
+
+// Rows the approximate stats take: k <= 128 (the tail's scratch holds both
+// term arrays), T in [2^-17, 2^20] and |xmax| <= 2^60 (x c + g cannot overflow
+// near the max), |taux| >= 2^-60 (quotients near the threshold are normal, so
+// the 2^-21 step below taux clears every tie).
+constexpr int kApproxMaxK = 128;
+__device__ __forceinline__ bool approx_row_ok(const RowP &rp, float xmax, float taux) {
+  return rp.k <= kApproxMaxK && rp.T >= 0x1p-17f && rp.T <= 0x1p20f && fabsf(xmax) <= 0x1p60f &&
+         fabsf(taux) >= 0x1p-60f;
 }
 
 // The r-th largest of the warp's 32 lane maxima (r <= 32), by a bitonic sort.
@@ -539,7 +678,10 @@ __device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHea
                                            const RawP &raw, const RowP &rp,
                                            unsigned long long *sk, float *scr, int lane);
 
-template <int JJ, bool BF16, bool EXACT, bool SELECT>
+// APPROX: rows that approx_row_ok accepts take stats_row_approx and are marked
+// approximate in their header; the others (and every row when APPROX is off)
+// take the exact stats_row. APPROX kernels need a.finite == nullptr (no row min).
+template <int JJ, bool BF16, bool EXACT, bool SELECT, bool APPROX>
 __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
     sample_stats_kernel(const KArgs a, RowHead *heads, RowCands *cands, int stages, int span) {
   extern __shared__ __align__(128) unsigned char dsm[];
@@ -594,13 +736,15 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       q2[j] = make_float2(x0, x1);
       pm[0] = max_nan(pm[0], x0);
       pm[1] = max_nan(pm[1], x1);
-      if (v0) pmn = fminf(pmn, x0);
-      if (v1) pmn = fminf(pmn, x1);
+      if (!APPROX) {
+        if (v0) pmn = fminf(pmn, x0);
+        if (v1) pmn = fminf(pmn, x1);
+      }
     }
     {
       const float lm = max_nan(pm[0], pm[PP - 1]);
       const float wm = warp_max_nan(lm);
-      const float wi = -warp_max(-pmn);
+      const float wi = APPROX ? 0.0f : -warp_max(-pmn);
       // candidate threshold in x: the ceil(k/4)-th largest lane maximum of this
       // warp (each of those lanes holds an element at least that large); x / T
       // is monotone, so the threshold in q is RN(min over warps / T)
@@ -626,7 +770,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       failed = true;
       break;
     }
-    if (a.finite && t == 0) {  // every logit finite: no NaN, and the max and min are finite
+    if (!APPROX && a.finite && t == 0) {  // every logit finite: no NaN, and the max and min are finite
       float fx = sm.red_max[par][0], fn = sm.red_min[par][0];
 #pragma unroll
       for (int i = 1; i < kFastW; ++i) {
@@ -645,19 +789,29 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
         taux = fminf(taux, sm.red_tau[par][i]);
       }
       // the row's four quotients in one divide across lanes: max (max(x / T) =
-      // RN(max(x) / T), RN being monotone), threshold, min, and 1 / T (= RN(1 / T))
-      const float num = lane == 0 ? xmax : (lane == 1 ? taux : (lane == 2 ? xmin : 1.0f));
+      // RN(max(x) / T), RN being monotone), threshold, min (APPROX: log2(e) / T),
+      // and 1 / T (= RN(1 / T))
+      const float num = lane == 0 ? xmax : (lane == 1 ? taux : (lane == 2 ? (APPROX ? kL2E : xmin) : 1.0f));
       const float quo = __fdiv_rn(num, rp.T);
       const float gmax = __shfl_sync(kFull, quo, 0);
       const float tau = __shfl_sync(kFull, quo, 1);
-      const float xminq = __shfl_sync(kFull, quo, 2);
+      const float q2nd = __shfl_sync(kFull, quo, 2);
       const float rT = __shfl_sync(kFull, quo, 3);
-      if (fabsf(gmax) < f_inf())
+      if (!(fabsf(gmax) < f_inf())) {
+        if (t == 0) {  // NaN, +inf, or every value -inf
+          flag_row(a, row, D3S_ROW_NONFINITE);
+          H.done = 1;
+        }
+      } else if (APPROX && approx_row_ok(rp, xmax, taux)) {
+        stats_row_approx<JJ, BF16>(H, cands[row], &sm.cand_n[s], rb, q2, q2nd,
+                                   __fmul_rn(-xmax, q2nd),
+                                   __fmaf_rn(-fabsf(taux), 0x1p-21f, taux), gmax, t, lane, w);
+      } else if (APPROX) {  // no row min here: the IEEE divide per element and the term floor
         stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q2, rp.T, rT, gmax, tau,
-                                   xminq, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);
-      else if (t == 0) {  // NaN, +inf, or every value -inf
-        flag_row(a, row, D3S_ROW_NONFINITE);
-        H.done = 1;
+                                   -f_inf(), false, t, lane, w);
+      } else {
+        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q2, rp.T, rT, gmax, tau,
+                                   q2nd, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);
       }
     } else if (t == 0) {
       if (pst != D3S_ROW_OK)
@@ -901,7 +1055,13 @@ __device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHea
     if (lane == 0) defer_row(a, row);
     return;
   }
-  const float lse = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
+  float lse_lo, lse_hi;
+  if (H.approx) {
+    lse_bounds(S, H.gmax, lse_lo, lse_hi);
+  } else {
+    lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
+    lse_hi = lse_lo;
+  }
   const uint2 key = raw_key(a, raw, lane);
   if (C <= 32)
     sort_cands<1>(cs, Cs, C, rp.k, rp.T, sk, lane);
@@ -911,8 +1071,15 @@ __device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHea
     sort_cands<4>(cs, Cs, C, rp.k, rp.T, sk, lane);
   else
     select_cands(Cs, C, rp.k, rp.T, sk, lane);
-  __syncwarp();
-  sample_tail(a, row, key, sk, scr, rp.k, lse, rp.p, lane);
+  // a cut the approximate sum leaves uncertain is decided by the exact sum (a
+  // second pass through the same tail)
+  for (;;) {
+    __syncwarp();
+    if (sample_tail(a, row, key, sk, scr, rp.k, lse_lo, lse_hi, rp.p, lane)) break;
+    const unsigned long long Se = exact_row_sum(a, row, rp.T, H.gmax, lane);
+    lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
+    lse_hi = lse_lo;
+  }
 }
 
 __global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KArgs a,
@@ -1066,15 +1233,6 @@ __device__ __forceinline__ void rw_pass2(const unsigned char *stage, int lane, i
       if (v1 && q.y >= tau) bits[(b + 1) >> 6] |= 1ull << ((b + 1) & 63);
     }
   }
-}
-
-// Sum over the warp of each lane's fixed-point total (< 2^55): three 21/21/22-bit
-// pieces, each summed exactly by a 32-bit redux.
-__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
-  const unsigned p0 = __reduce_add_sync(kFull, (unsigned)(v & 0x1FFFFFu));
-  const unsigned p1 = __reduce_add_sync(kFull, (unsigned)((v >> 21) & 0x1FFFFFu));
-  const unsigned p2 = __reduce_add_sync(kFull, (unsigned)(v >> 42));
-  return (unsigned long long)p0 + ((unsigned long long)p1 << 21) + ((unsigned long long)p2 << 42);
 }
 
 // Warps that fit on an SM: the f32 rows of the largest chunk counts are held
@@ -1250,7 +1408,7 @@ __global__ void __launch_bounds__(32, RwBounds<NC>::kMinBlocks)
       else
         select_list(cs, C, k, lane);
       __syncwarp();
-      sample_tail(a, row, raw_key(a, cur, lane), cs, scr, k, lse, rp.p, lane);
+      sample_tail(a, row, raw_key(a, cur, lane), cs, scr, k, lse, lse, rp.p, lane);
     }
     __syncwarp();
   }
@@ -1354,7 +1512,7 @@ __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a
         __syncthreads();
       }
     }
-    if (w == 0) sample_tail(a, row, row_key(a, row), keys, scr, k, lse, rp.p, lane);
+    if (w == 0) sample_tail(a, row, row_key(a, row), keys, scr, k, lse, lse, rp.p, lane);
     __syncthreads();
   }
   if (use_list) {
@@ -1388,7 +1546,8 @@ __global__ void math_kernel(int op, const float *x, float *y, int64_t n, float T
       case 0: r = exp_full(v); break;
       case 1: r = log_full(v); break;
       case 2: r = exp_term(v); break;
-      default: r = div_rows(v, __frcp_rn(T), -T); break;
+      case 3: r = div_rows(v, __frcp_rn(T), -T); break;
+      default: r = ex2_approx(v); break;
     }
     y[i] = r;
   }
@@ -1426,15 +1585,30 @@ using StatFn = void (*)(const KArgs, RowHead *, RowCands *, int, int);
 template <bool BF16, bool EXACT, bool SELECT>
 StatFn pick_stats_e(int J) {
   switch (J) {
-    case 1: return sample_stats_kernel<1, BF16, EXACT, SELECT>;
-    case 2: return sample_stats_kernel<2, BF16, EXACT, SELECT>;
-    case 4: return sample_stats_kernel<4, BF16, EXACT, SELECT>;
-    case 8: return sample_stats_kernel<8, BF16, EXACT, SELECT>;
-    case 12: return sample_stats_kernel<12, BF16, EXACT, SELECT>;
-    case 16: return sample_stats_kernel<16, BF16, EXACT, SELECT>;
-    case 17: return sample_stats_kernel<17, BF16, EXACT, SELECT>;
-    case 24: return sample_stats_kernel<24, BF16, EXACT, SELECT>;
-    case 32: return sample_stats_kernel<32, BF16, EXACT, SELECT>;
+    case 1: return sample_stats_kernel<1, BF16, EXACT, SELECT, false>;
+    case 2: return sample_stats_kernel<2, BF16, EXACT, SELECT, false>;
+    case 4: return sample_stats_kernel<4, BF16, EXACT, SELECT, false>;
+    case 8: return sample_stats_kernel<8, BF16, EXACT, SELECT, false>;
+    case 12: return sample_stats_kernel<12, BF16, EXACT, SELECT, false>;
+    case 16: return sample_stats_kernel<16, BF16, EXACT, SELECT, false>;
+    case 17: return sample_stats_kernel<17, BF16, EXACT, SELECT, false>;
+    case 24: return sample_stats_kernel<24, BF16, EXACT, SELECT, false>;
+    case 32: return sample_stats_kernel<32, BF16, EXACT, SELECT, false>;
+    default: return nullptr;
+  }
+}
+
+// The approximate-sum stats kernels (large batches; the long rows that reach
+// the stats + select pair have J >= 8).
+template <bool BF16, bool EXACT>
+StatFn pick_stats_approx_e(int J) {
+  switch (J) {
+    case 8: return sample_stats_kernel<8, BF16, EXACT, false, true>;
+    case 12: return sample_stats_kernel<12, BF16, EXACT, false, true>;
+    case 16: return sample_stats_kernel<16, BF16, EXACT, false, true>;
+    case 17: return sample_stats_kernel<17, BF16, EXACT, false, true>;
+    case 24: return sample_stats_kernel<24, BF16, EXACT, false, true>;
+    case 32: return sample_stats_kernel<32, BF16, EXACT, false, true>;
     default: return nullptr;
   }
 }
@@ -1443,6 +1617,12 @@ template <bool BF16, bool SELECT>
 StatFn pick_stats(int J, int V) {
   return J == (V + kPartials - 1) / kPartials ? pick_stats_e<BF16, true, SELECT>(J)
                                               : pick_stats_e<BF16, false, SELECT>(J);
+}
+
+template <bool BF16>
+StatFn pick_stats_approx(int J, int V) {
+  return J == (V + kPartials - 1) / kPartials ? pick_stats_approx_e<BF16, true>(J)
+                                              : pick_stats_approx_e<BF16, false>(J);
 }
 
 int pick_J(int V) {
@@ -1532,7 +1712,9 @@ int launch_fast(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStr
   int stages = BF16 ? 3 : 2;
   while (stages > 2 && (size_t)stages * span > 64 * 1024) --stages;
   const size_t smem = (size_t)stages * span;
-  StatFn fn = pick_stats<BF16, false>(J, a.V);
+  // the approximate full-row sum unless the caller wants per-row finite flags
+  StatFn fn = a.finite ? nullptr : pick_stats_approx<BF16>(J, a.V);
+  if (!fn) fn = pick_stats<BF16, false>(J, a.V);
   if (!fn) return D3S_ERR_ARG;
   const int occ = prepare((const void *)fn, kFastThreads, smem);
   const int sms = device_sms();

@@ -50,9 +50,9 @@ struct KArgs {
 // in a separate slab.
 struct alignas(16) RowHead {
   float gmax;
-  int done;  // 1: the stats kernel already wrote the row's result (or handed it on)
-  int cnt;   // candidates (the first min(cnt, 256) are stored)
-  int pad;
+  int done;    // 1: the stats kernel already wrote the row's result (or handed it on)
+  int cnt;     // candidates (the first min(cnt, 256) are stored)
+  int approx;  // 1: sum[] holds the SFU-exp2 approximation of the full-row sum
   unsigned long long sum[4];
 };
 struct alignas(16) RowCands {

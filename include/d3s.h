@@ -157,7 +157,8 @@ D3S_API int d3s_ctx_check(d3s_ctx *ctx);
 
 /* Test hooks (no counterpart in the reference): y_dev = f(x_dev) with the
  * kernels' own arithmetic; op 0 = exp, 1 = log, 2 = the full-row-sum term
- * exp(max(x, -86)), 3 = x / param by the per-row reciprocal path. */
+ * exp(max(x, -86)), 3 = x / param by the per-row reciprocal path, 4 = the
+ * special-function unit's 2^x that the approximate full-row sum uses. */
 D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
                            float param, void *stream);
 /* Counts float bit patterns x in [lo, hi) (step `step`) with |x| in

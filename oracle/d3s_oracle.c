@@ -436,6 +436,67 @@ done:
   return result;
 }
 
+int d3o_row_cums(const float *x, int V, float temperature, int k, float *cums) {
+  if (temperature < D3O_MIN_TEMPERATURE) temperature = D3O_MIN_TEMPERATURE;
+  float *q = malloc(sizeof(float) * (size_t)V);
+  float *vals = malloc(sizeof(float) * (size_t)k);
+  int32_t *ids = malloc(sizeof(int32_t) * (size_t)k);
+  float gmax = -INFINITY;
+  for (int i = 0; i < V; i++) {
+    q[i] = x[i] / temperature;
+    if (q[i] > gmax) gmax = q[i];
+  }
+  uint64_t S = 0;
+  int bad = 0;
+  for (int p = 0; p < D3O_PARTIALS && p < V; p++) {
+    float s = 0.0f;
+    for (int i = p; i < V; i += D3O_PARTIALS) s = s + d3o_exp_term(q[i] - gmax);
+    if (s != s)
+      bad = 1;
+    else
+      S += (uint64_t)(s * 0x1p46f);
+  }
+  if (!bad) {
+    float lse = gmax + d3o_log((float)S * 0x1p-46f);
+    d3o_topk_stable(q, V, k, vals, ids);
+    float cum = 0.0f;
+    for (int r = 0; r < k; r++) {
+      cum = cum + d3o_exp(vals[r] - lse);
+      cums[r] = cum;
+    }
+  }
+  free(q);
+  free(vals);
+  free(ids);
+  return bad ? -1 : 0;
+}
+
+double d3o_exp_max_relerr(float lo, float hi) {
+  double worst = 0.0;
+  const uint32_t b_lo = f2u(hi) | 0x80000000u, b_hi = f2u(lo); /* -|hi| .. -|lo|, bits ascending */
+#ifdef _OPENMP
+#pragma omp parallel for reduction(max : worst) schedule(static)
+#endif
+  for (int64_t b = (int64_t)b_lo; b <= (int64_t)b_hi; b++) {
+    const float d = u2f((uint32_t)b);
+    const double r = exp((double)d);
+    const double e = fabs((double)d3o_exp(d) - r) / r;
+    if (e > worst) worst = e;
+  }
+  return worst;
+}
+
+int64_t d3o_log_nonmonotone(float lo, float hi) {
+  int64_t bad = 0;
+  const uint32_t b_lo = f2u(lo), b_hi = f2u(hi);
+#ifdef _OPENMP
+#pragma omp parallel for reduction(+ : bad) schedule(static)
+#endif
+  for (int64_t b = (int64_t)b_lo; b < (int64_t)b_hi; b++)
+    if (d3o_log(u2f((uint32_t)b + 1u)) < d3o_log(u2f((uint32_t)b))) bad++;
+  return bad;
+}
+
 static void row_to_f32(const void *logits, int dtype, int64_t ld, int row, int V, float *dst) {
   if (dtype == D3O_BF16) {
     const uint16_t *src = (const uint16_t *)logits + (int64_t)row * ld;

@@ -87,6 +87,17 @@ typedef struct {
 int d3o_sample_row(const float *x, int V, float temperature, float top_p, int k,
                    const float *u, int32_t *topk_ids, float *probs, d3o_diag *diag);
 
+/* Test support: the inclusive cumsums cum_r (r < k) that sample_fn compares
+ * with top_p (src/sampling.c:39-43), without the cut, for a finite row.
+ * Returns 0, or -1 for a non-finite row. */
+int d3o_row_cums(const float *x, int V, float temperature, int k, float *cums);
+
+/* Test support: the largest relative error of d3o_exp against double exp over
+ * every float in [lo, hi] (lo <= hi <= 0, results normal), and the number of
+ * adjacent floats a < b in [lo, hi] (0 < lo) with d3o_log(b) < d3o_log(a). */
+double d3o_exp_max_relerr(float lo, float hi);
+int64_t d3o_log_nonmonotone(float lo, float hi);
+
 /* Top k of q [V] in the order of the Metal kernel's selection + merge
  * (src/sampling.c:93-121). vals / ids [k]. */
 void d3o_topk_metal_order(const float *q, int V, int k, float *vals, int32_t *ids);

@@ -127,6 +127,12 @@ def lib():
                                      ctypes.c_float, ctypes.c_int, _u32p, _u32p, _i32p,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      _i32p, _i32p, _i32p]
+        L.d3o_row_cums.restype = ctypes.c_int
+        L.d3o_row_cums.argtypes = [_f32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, _f32p]
+        L.d3o_exp_max_relerr.restype = ctypes.c_double
+        L.d3o_exp_max_relerr.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.d3o_log_nonmonotone.restype = ctypes.c_int64
+        L.d3o_log_nonmonotone.argtypes = [ctypes.c_float, ctypes.c_float]
         L.d3o_history_push.argtypes = [_i32p, ctypes.POINTER(ctypes.c_int), ctypes.c_int32]
         _lib = L
     return _lib
@@ -233,6 +239,25 @@ def sample_row(x: np.ndarray, temperature: float, top_p: float, k: int, u: np.nd
     r = lib().d3o_sample_row(_p(x, _f32p), x.size, temperature, top_p, k, _p(u, _f32p),
                              _p(ids, _i32p), _p(probs, _f32p), ctypes.byref(d))
     return r, ids, probs, d
+
+
+def row_cums(x: np.ndarray, temperature: float, k: int) -> np.ndarray:
+    """The inclusive cumsums [k] the top-p rule compares with top_p (no cut)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(k, np.float32)
+    rc = lib().d3o_row_cums(_p(x, _f32p), x.size, temperature, k, _p(out, _f32p))
+    assert rc == 0, "non-finite row"
+    return out
+
+
+def exp_max_relerr(lo: float, hi: float) -> float:
+    """Largest relative error of the oracle's exp over every float in [lo, hi] (<= 0)."""
+    return float(lib().d3o_exp_max_relerr(lo, hi))
+
+
+def log_nonmonotone(lo: float, hi: float) -> int:
+    """Adjacent float pairs in [lo, hi) where the oracle's log decreases."""
+    return int(lib().d3o_log_nonmonotone(lo, hi))
 
 
 def topk_stable(q: np.ndarray, k: int):

@@ -370,3 +370,74 @@ def test_full_size_config5(ctx, oracle, synth):
                               k[rows_t].cpu().numpy(), seeds[rows_t].cpu().numpy().astype(np.uint64))
     assert ids[rows_t].cpu().numpy().tolist() == want.tolist()
     ctx.check()
+
+
+# ---- the approximate full-row sum of large batches and its certified cut ----
+
+def test_ex2_approx_error_bound(ctx):
+    """Large batches sum each row with the SFU's exp2; the error bound carried
+    into the top-p cut assumes its relative error is below 2^-22.5 wherever the
+    result is normal. Checked over every float input in [-127, 2^-8]."""
+    worst = 0.0
+    for lo, hi in [(0x80000000, 0xC2FE0001), (0x00000000, 0x3B800001)]:
+        for s in range(lo, hi, 1 << 26):
+            e = min(s + (1 << 26), hi)
+            x = torch.arange(s, e, dtype=torch.int64, device="cuda").to(torch.int32).view(torch.float32)
+            y = ctx.debug_math(4, x).double()
+            ref = torch.exp2(x.double())
+            normal = ref >= 2.0 ** -126
+            worst = max(worst, float(((y - ref).abs() / ref)[normal].max()))
+            del x, y, ref, normal
+    assert worst < 2.0 ** -22.5, worst
+
+
+def test_top_p_on_a_cumsum_takes_the_exact_sum(ctx, oracle):
+    """Rows whose top_p sits exactly on one of their cumsums, or one float
+    below it, leave the cut uncertain under the approximate sum's error bound:
+    the kernel recomputes those rows' exact sums. Ids, kept counts and
+    probabilities must equal the oracle's on every row of a large batch."""
+    import d3s
+    rng = np.random.default_rng(21)
+    N, V, k = 2600, 4097, 48
+    x = (rng.standard_normal((N, V)) * 3).astype(np.float32)
+    T = rng.uniform(0.5, 1.2, N).astype(np.float32)
+    p = rng.uniform(0.5, 1.0, N).astype(np.float32)
+    special = rng.choice(N, 400, replace=False)
+    for i, r in enumerate(special):
+        cums = oracle.row_cums(x[r], float(T[r]), k)
+        c = np.float32(cums[int(rng.integers(1, k))])
+        p[r] = c if i % 2 == 0 else np.nextafter(c, np.float32(0.0))
+    u = rng.random((N, k), dtype=np.float32)
+    ids = torch.empty(N, dtype=torch.int32, device="cuda")
+    kept, status = torch.empty_like(ids), torch.empty_like(ids)
+    probs = torch.zeros(N, k, dtype=torch.float32, device="cuda")
+    req = ctx.request(dev(x), ids, temperature_rows=dev(T), top_p_rows=dev(p), top_k=k,
+                      noise=d3s.NOISE_GIVEN, u=dev(u), status=status, kept=kept, probs=probs)
+    ctx.sample(req)
+    got_ids, got_kept, got_probs = ids.cpu().numpy(), kept.cpu().numpy(), probs.cpu().numpy()
+    for r in range(N):
+        rid, _, oprobs, d = oracle.sample_row(x[r], float(T[r]), float(p[r]), k, u[r])
+        assert got_ids[r] == rid and got_kept[r] == d.kept, r
+        assert got_probs[r].view(np.uint32).tolist() == oprobs.view(np.uint32).tolist(), r
+    ctx.check()
+
+
+def test_rows_outside_the_approximate_path(ctx, oracle):
+    """In a large batch, rows the approximate sum does not take (k > 128, T
+    above 2^20, |x| above 2^60) run the exact per-element path in the same
+    kernel; every row must equal the oracle."""
+    rng = np.random.default_rng(22)
+    N, V = 2600, 4097
+    x = (rng.standard_normal((N, V)) * 3).astype(np.float32)
+    T = rng.uniform(0.5, 1.2, N).astype(np.float32)
+    p = rng.uniform(0.5, 1.0, N).astype(np.float32)
+    k = rng.integers(1, 65, N).astype(np.int32)
+    k[::5] = rng.integers(129, 257, len(k[::5]))
+    T[1::7] = 2.0 ** 21
+    x[3::11] *= np.float32(2.0 ** 61)
+    seeds = np.arange(N, dtype=np.int64) * 5 + 1
+    ids = torch.empty(N, dtype=torch.int32, device="cuda")
+    ctx.sample_rows(dev(x), ids, temperature=dev(T), top_p=dev(p), top_k=dev(k), seeds=dev(seeds))
+    want = oracle.sample_rows(x, T, p, k, seeds.astype(np.uint64))
+    assert ids.cpu().numpy().tolist() == want.tolist()
+    ctx.check()

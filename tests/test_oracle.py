@@ -142,6 +142,16 @@ def test_log_accuracy(oracle):
     assert abs(sp[4] - math.log(float(np.float32(1e-45)))) < 1e-4  # smallest subnormal
 
 
+def test_exp_and_log_facts_the_certified_cut_uses(oracle):
+    """The large-batch kernels sum a row with the SFU's exp2 and carry the error
+    bound into the top-p cut. That bound assumes exp's relative error is below
+    2^-23.5 over every float of [-86, 0] (the full-row-sum terms and the cumsum
+    terms), and it brackets lse through log, which must never decrease over
+    [1, 16384) (the normalised sum S / 2^46 of rows up to 8192 long)."""
+    assert oracle.exp_max_relerr(-86.0, 0.0) < 2.0 ** -23.5
+    assert oracle.log_nonmonotone(1.0, 16384.0) == 0
+
+
 # ---- the sampler ----
 
 def kept_set_definition(x, T, k, p):

@@ -22,6 +22,7 @@
 // from global memory (L2) in each pass, selection by exact bisection on the
 // 64-bit (value, id) key, bitonic sort of the k winners in shared memory.
 #include <algorithm>
+#include <cmath>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -361,44 +362,23 @@ __device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v)
   return (unsigned long long)p0 + ((unsigned long long)p1 << 21) + ((unsigned long long)p2 << 42);
 }
 
-// The exact full-row sum of a finite row, by one warp, read back from global
-// memory: partial p (lane p % 32 holds it) is the sequential float sum of
-// exp(max(x_i / T - gmax, -86)) over i = p, p + 256, ..., truncated to 2^-46
-// fixed point; the partials are added exactly (the oracle's definition).
-// Only rows whose approximate sum left the top-p cut uncertain come here.
-__device__ __forceinline__ unsigned long long exact_row_sum(const KArgs &a, int row, float T,
-                                                         float gmax, int lane) {
-  const int V = a.V;
-  const int64_t off = phys_row(a, row) * a.ld;
-  const bool bf16 = a.dtype == D3S_BF16;
-  unsigned long long fx = 0ull;
-  for (int p = lane; p < kPartials && p < V; p += 32) {
-    float s = 0.0f;
-    for (int i = p; i < V; i += kPartials) {
-      const float x = bf16 ? load_x<true>(a.logits, off + i) : load_x<false>(a.logits, off + i);
-      s = __fadd_rn(s, exp_term(__fsub_rn(__fdiv_rn(x, T), gmax)));
-    }
-    fx += __float2ull_rz(__fmul_rn(s, 0x1p46f));
-  }
-  return warp_sum_u64(fx);
-}
-
 // Bounds on the exact lse of a row from its approximate full-row sum S (2^-46
 // fixed point, the SFU's exp2 of RN(x c + g) with c = RN(log2(e) / T) and
 // g = RN(-xmax c)).
-// With G = |max x / T| and V <= 8192, first-order error analysis bounds
-// |S_exact - S| / S by 2^-24 (3 G + 5 ln V + n_p + L + 1) + e_exp + e_ex2:
-// the quotients' and differences' roundings (2G + 2 ln V for the exact sum,
-// G + 3 ln V for the approximate one, ln V bounding the entropy-weighted |x/T -
-// max|), sequential sums of n_p <= 32 and L <= 32 terms, exp's relative error
-// (below 2^-23.5) and ex2.approx's (below 2^-22.5; both checked by the tests).
-// Rounded up: 2^-24 (3.1 G + 128). The
-// exact lse = RN(gmax + log(RN(S_exact) 2^-46)) is then bracketed by the same
-// expression at the bracket's ends: RN and log are monotone there (log is
-// checked over every float in [1, 16384) by the tests).
-__device__ __forceinline__ void lse_bounds(unsigned long long S, float gmax, float &lse_lo,
-                                           float &lse_hi) {
-  const float delta = __fmaf_ru(0x1.8cccccp-23f, fabsf(gmax), 0x1p-17f);
+// With G = |max x / T|, first-order error analysis bounds |S_exact - S| / S by
+// 2^-24 (3 G + 5 ln V + n_p + L + 1) + e_exp + e_ex2: the quotients' and
+// differences' roundings (2G + 2 ln V for the exact sum, G + 3 ln V for the
+// approximate one, ln V bounding the entropy-weighted |x/T - max|), sequential
+// sums of n_p (the exact partials) and L (the approximate accumulators) terms,
+// exp's relative error (below 2^-23.5) and ex2.approx's (below 2^-22.5; both
+// checked by the tests). approx_bound_c0 rounds the row-independent part up;
+// the row's part is 3.1 G 2^-24. The exact lse = RN(gmax + log(RN(S_exact)
+// 2^-46)) is then bracketed by the same expression at the bracket's ends: RN
+// and log are monotone there (log is checked over every float in [1, 16384) by
+// the tests).
+__device__ __forceinline__ void lse_bounds(unsigned long long S, float gmax, float c0,
+                                           float &lse_lo, float &lse_hi) {
+  const float delta = __fmaf_ru(0x1.8cccccp-23f, fabsf(gmax), c0);
   const float lo = __fmul_rd(__fmul_rd(__ull2float_rd(S), __fsub_rd(1.0f, delta)), 0x1p-46f);
   const float hi = __fmul_ru(__fmul_ru(__ull2float_ru(S), __fadd_ru(1.0f, delta)), 0x1p-46f);
   lse_lo = __fadd_rn(gmax, log_full(fmaxf(lo, 1.0f)));  // the exact S is at least 2^46
@@ -487,6 +467,16 @@ __device__ __forceinline__ void defer_row(const KArgs &a, int row) {
   const unsigned pos = atomicAdd(a.deferred_n, 1u);
   if (pos < (unsigned long long)a.deferred_cap)
     a.deferred[pos] = row;
+  else
+    flag_row(a, row, D3S_ROW_BADPARAM);
+}
+// Hand a row whose top-p cut the approximate sum could not certify to the wide
+// kernel, which recomputes the exact full-row sum with a whole CTA and then
+// samples the row from its stored candidates. Stored as -(row + 1).
+__device__ __forceinline__ void defer_row_exact_sum(const KArgs &a, int row) {
+  const unsigned pos = atomicAdd(a.deferred_n, 1u);
+  if (pos < (unsigned long long)a.deferred_cap)
+    a.deferred[pos] = -(row + 1);
   else
     flag_row(a, row, D3S_ROW_BADPARAM);
 }
@@ -673,7 +663,7 @@ __device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k, f
 
 // The select kernel's work on one row whose record is complete: the row's
 // lse, its subkey, the top k of its candidates in rank order in sk, the tail.
-__device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHead &H,
+__device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHead &H,
                                            const unsigned long long *cs, const RowCands &Cs,
                                            const RawP &raw, const RowP &rp,
                                            unsigned long long *sk, float *scr, int lane);
@@ -842,7 +832,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       // sorted keys and the tail's scratch.
       __syncthreads();
       if (w == 0 && !H.done)
-        select_row(a, row, H, cands[row].cand, cands[row], cur, rp,
+        (void)select_row(a, row, H, cands[row].cand, cands[row], cur, rp,
                    reinterpret_cast<unsigned long long *>(dsm),
                    reinterpret_cast<float *>(dsm + kCandCap * 8), lane);
     }
@@ -864,6 +854,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
 
 constexpr int kSelWarps = 8;
 constexpr int kSelThreads = 32 * kSelWarps;
+constexpr int kSelExactRows = 16;  // rows per CTA that wait for the exact sum at the end
 constexpr int kStageCands = 128;  // candidates staged in shared memory per row
 
 __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
@@ -1043,7 +1034,23 @@ __device__ __forceinline__ void stage_row(const RowHead *heads, const RowCands *
                reinterpret_cast<const char *>(cands + row) + 16 * c);
 }
 
-__device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHead &H,
+// The top k of a row's C <= 256 candidates (the first kStageCands in cs, all of
+// them in Cs), keyed by their exact quotients, in rank order into sk.
+__device__ __forceinline__ void rank_cands(const unsigned long long *cs, const RowCands &Cs, int C,
+                                           int k, float T, unsigned long long *sk, int lane) {
+  if (C <= 32)
+    sort_cands<1>(cs, Cs, C, k, T, sk, lane);
+  else if (C <= 64)
+    sort_cands<2>(cs, Cs, C, k, T, sk, lane);
+  else if (C <= 128)
+    sort_cands<4>(cs, Cs, C, k, T, sk, lane);
+  else
+    select_cands(Cs, C, k, T, sk, lane);
+}
+
+// Returns false, having written nothing, when the row's top-p cut needs the
+// exact full-row sum (an approximate-sum row whose cut is uncertain).
+__device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHead &H,
                                            const unsigned long long *cs, const RowCands &Cs,
                                            const RawP &raw, const RowP &rp,
                                            unsigned long long *sk, float *scr, int lane) {
@@ -1053,42 +1060,33 @@ __device__ __forceinline__ void select_row(const KArgs &a, int row, const RowHea
   for (int i = 0; i < kFastW; ++i) S += H.sum[i];
   if (C > kCandCap) {  // more candidates than the list holds (ties): the wide kernel's exact path
     if (lane == 0) defer_row(a, row);
-    return;
+    return true;
   }
   float lse_lo, lse_hi;
   if (H.approx) {
-    lse_bounds(S, H.gmax, lse_lo, lse_hi);
+    lse_bounds(S, H.gmax, a.approx_c0, lse_lo, lse_hi);
   } else {
     lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
     lse_hi = lse_lo;
   }
   const uint2 key = raw_key(a, raw, lane);
-  if (C <= 32)
-    sort_cands<1>(cs, Cs, C, rp.k, rp.T, sk, lane);
-  else if (C <= 64)
-    sort_cands<2>(cs, Cs, C, rp.k, rp.T, sk, lane);
-  else if (C <= 128)
-    sort_cands<4>(cs, Cs, C, rp.k, rp.T, sk, lane);
-  else
-    select_cands(Cs, C, rp.k, rp.T, sk, lane);
-  // a cut the approximate sum leaves uncertain is decided by the exact sum (a
-  // second pass through the same tail)
-  for (;;) {
-    __syncwarp();
-    if (sample_tail(a, row, key, sk, scr, rp.k, lse_lo, lse_hi, rp.p, lane)) break;
-    const unsigned long long Se = exact_row_sum(a, row, rp.T, H.gmax, lane);
-    lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
-    lse_hi = lse_lo;
-  }
+  rank_cands(cs, Cs, C, rp.k, rp.T, sk, lane);
+  __syncwarp();
+  return sample_tail(a, row, key, sk, scr, rp.k, lse_lo, lse_hi, rp.p, lane);
 }
 
-__global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KArgs a,
+__global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KArgs a,
                                                                         const RowHead *heads,
                                                                         const RowCands *cands) {
   __shared__ __align__(16) float scr_all[kSelWarps][kFastMaxK + 4];
   __shared__ unsigned long long sk_all[kSelWarps][kFastMaxK];
   __shared__ SelStage stg_all[kSelWarps][2];
+  __shared__ int exact_rows[kSelExactRows];
+  __shared__ unsigned exact_n;
+  __shared__ unsigned long long exact_red[kSelWarps];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (threadIdx.x == 0) exact_n = 0u;
+  __syncthreads();
   const int gw = blockIdx.x * kSelWarps + w, nw = gridDim.x * kSelWarps;
   unsigned long long *sk = sk_all[w];
   int row = gw, b = 0;
@@ -1119,10 +1117,68 @@ __global__ void __launch_bounds__(kSelThreads, 5) sample_select_kernel(const KAr
     if (!st.head.done) {
       RowP rp;
       resolve(a, raw, rp);  // valid: the stats kernel flagged every other row
-      select_row(a, row, st.head, st.cand, cands[row], raw, rp, sk, scr_all[w], lane);
+      if (!select_row(a, row, st.head, st.cand, cands[row], raw, rp, sk, scr_all[w], lane) &&
+          lane == 0) {
+        const unsigned pos = atomicAdd(&exact_n, 1u);
+        if (pos < (unsigned)kSelExactRows)
+          exact_rows[pos] = row;
+        else
+          defer_row_exact_sum(a, row);
+      }
     }
     raw = rawn;
     cnt_next = cnt_nn;
+  }
+  // The rows whose cut needed the exact full-row sum, by the whole CTA once its
+  // warps are done: thread t computes partial t (256 threads, 256 partials) of
+  // the oracle's definition, then warp 0 ranks the row's stored candidates and
+  // runs the tail with the exact lse. Few rows per launch come here (the cut
+  // must fall within about 1e-5 of top_p); doing them last keeps their reads of
+  // the row (long evicted from L2) off every warp's critical path but one.
+  static_assert(kSelThreads == kPartials, "one partial per thread");
+  __syncthreads();
+  const unsigned n_exact = min(exact_n, (unsigned)kSelExactRows);
+  for (unsigned e = 0; e < n_exact; ++e) {
+    const int xrow = exact_rows[e];
+    RowP rp;
+    row_params(a, xrow, rp);
+    const RowHead &H = heads[xrow];
+    const float gmax = H.gmax;
+    const int64_t off = phys_row(a, xrow) * a.ld;
+    const bool bf16 = a.dtype == D3S_BF16;
+    const float rT = __frcp_rn(rp.T), mT = -rp.T;
+    const bool recip = rp.T >= 0x1p-17f && rp.T <= 0x1p20f;  // div_rows' exact range of T
+    float xv[kFastMaxV / kPartials];
+#pragma unroll
+    for (int j = 0; j < kFastMaxV / kPartials; ++j) {
+      const int i = threadIdx.x + kPartials * j;
+      xv[j] = i < a.V ? (bf16 ? load_x<true>(a.logits, off + i) : load_x<false>(a.logits, off + i))
+                      : 0.0f;
+    }
+    float sp = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kFastMaxV / kPartials; ++j) {
+      if ((int)threadIdx.x + kPartials * j < a.V) {
+        const float ax = fabsf(xv[j]);
+        const float q = (recip && ax >= 0x1p-100f && ax <= 0x1p60f) ? div_rows(xv[j], rT, mT)
+                                                                     : __fdiv_rn(xv[j], rp.T);
+        sp = __fadd_rn(sp, exp_term(__fsub_rn(q, gmax)));
+      }
+    }
+    const unsigned long long ws = warp_sum_fixed(__float2ull_rz(__fmul_rn(sp, 0x1p46f)));
+    if (lane == 0) exact_red[w] = ws;
+    __syncthreads();
+    if (w == 0) {
+      unsigned long long Se = 0;
+#pragma unroll
+      for (int i = 0; i < kSelWarps; ++i) Se += exact_red[i];
+      const float lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
+      const RowCands &Cs = cands[xrow];
+      rank_cands(Cs.cand, Cs, H.cnt, rp.k, rp.T, sk, lane);
+      __syncwarp();
+      sample_tail(a, xrow, row_key(a, xrow), sk, scr_all[0], rp.k, lse, lse, rp.p, lane);
+    }
+    __syncthreads();
   }
 }
 
@@ -1416,9 +1472,15 @@ __global__ void __launch_bounds__(32, RwBounds<NC>::kMinBlocks)
 
 // ---- wide kernel ----
 
+// Rows on the hand-off list are processed in full (exact max, exact full-row
+// sum, exact k-th key by bisection, bitonic sort), except entries -(row + 1):
+// rows of the approximate-sum kernels whose cut needed the exact sum, which is
+// computed here (one partial per thread) before warp 0 ranks the row's stored
+// candidates (heads / cands) and runs the tail with the exact lse.
 template <bool BF16>
 __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a, int use_list,
-                                                                    int kcap) {
+                                                                    int kcap, const RowHead *heads,
+                                                                    const RowCands *cands) {
   extern __shared__ unsigned long long keys[];  // [pow2 >= kcap] keys, then float scr[kcap]
   __shared__ float red_max[kWideWarps];
   __shared__ unsigned long long red_sum[kWideWarps];
@@ -1433,7 +1495,9 @@ __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a
       use_list ? (unsigned)min((long long)*((volatile uint32_t *)a.deferred_n), (long long)a.deferred_cap)
                : (unsigned)a.N;
   for (unsigned idx = blockIdx.x; idx < nrows; idx += gridDim.x) {
-    const int row = use_list ? a.deferred[idx] : (int)idx;
+    const int entry = use_list ? a.deferred[idx] : (int)idx;
+    const bool exact_sum_only = entry < 0;
+    const int row = exact_sum_only ? -entry - 1 : entry;
     if (a.finite && !use_list) {  // (rows handed on by the stats kernel have theirs)
       const void *b0 = row_base<BF16>(a, row);
       bool fin = true;
@@ -1448,6 +1512,46 @@ __global__ void __launch_bounds__(kWideThreads) sample_wide_kernel(const KArgs a
       continue;
     }
     const int k = rp.k;
+    if (exact_sum_only) {
+      // A row of the stats kernels (V <= 8192, finite, its exact max in the
+      // header): thread t's partial, all of its <= 32 elements loaded at once
+      // (the row left L2 long ago), the reciprocal quotient where it is exact.
+      const void *b0 = row_base<BF16>(a, row);
+      const float gmax = heads[row].gmax;
+      float xv[kFastMaxV / kWideThreads];
+#pragma unroll
+      for (int j = 0; j < kFastMaxV / kWideThreads; ++j) {
+        const int i = t + kWideThreads * j;
+        xv[j] = i < V ? load_x<BF16>(b0, i) : 0.0f;
+      }
+      const float rT = __frcp_rn(rp.T), mT = -rp.T;
+      const bool recip = rp.T >= 0x1p-17f && rp.T <= 0x1p20f;
+      float sp = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kFastMaxV / kWideThreads; ++j) {
+        if (t + kWideThreads * j < V) {
+          const float ax = fabsf(xv[j]);
+          const float q = (recip && ax >= 0x1p-100f && ax <= 0x1p60f) ? div_rows(xv[j], rT, mT)
+                                                                       : __fdiv_rn(xv[j], rp.T);
+          sp = __fadd_rn(sp, exp_term(__fsub_rn(q, gmax)));
+        }
+      }
+      const unsigned long long ws = warp_sum_fixed(__float2ull_rz(__fmul_rn(sp, 0x1p46f)));
+      if (lane == 0) red_sum[w] = ws;
+      __syncthreads();
+      if (w == 0) {
+        unsigned long long Se = 0;
+#pragma unroll
+        for (int i = 0; i < kWideWarps; ++i) Se += red_sum[i];
+        const float lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
+        const RowCands &Cs = cands[row];
+        rank_cands(Cs.cand, Cs, heads[row].cnt, k, rp.T, keys, lane);
+        __syncwarp();
+        sample_tail(a, row, row_key(a, row), keys, scr, k, lse, lse, rp.p, lane);
+      }
+      __syncthreads();
+      continue;
+    }
     int kp = 1;
     while (kp < k) kp <<= 1;
     const void *base = row_base<BF16>(a, row);
@@ -1690,7 +1794,8 @@ size_t wide_smem(int kcap) {
 }
 
 template <bool BF16>
-int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st, int max_grid = 1 << 30) {
+int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st, int max_grid = 1 << 30,
+                const RowHead *heads = nullptr, const RowCands *cands = nullptr) {
   const size_t smem = wide_smem(kcap);
   auto fn = sample_wide_kernel<BF16>;
   const int occ = prepare((const void *)fn, kWideThreads, smem);
@@ -1700,13 +1805,25 @@ int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st, int max
   if (!use_list) grid = std::min(grid, a.N);
   grid = std::min(grid, max_grid);
   if (grid < 1) grid = 1;
-  fn<<<grid, kWideThreads, smem, st>>>(a, use_list, kcap);
+  fn<<<grid, kWideThreads, smem, st>>>(a, use_list, kcap, heads, cands);
   return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+}
+
+// The row-independent part of the approximate full-row sum's error bound (see
+// lse_bounds) for rows of V with J columns per stats thread, rounded up:
+// 2^-24 (1.01 (5 ln V + n_p + L + 1 + 6) + 1), where n_p = ceil(V / 256) and
+// L = J terms per accumulator.
+float approx_bound_c0(int V, int J) {
+  const double n_p = (double)((V + kPartials - 1) / kPartials);
+  const double units = 1.01 * (5.0 * std::log((double)V) + n_p + (double)J + 1.0 + 6.0) + 1.0;
+  return (float)std::ldexp(units, -24);
 }
 
 // The fast path: stats (K1) -> select (K2) -> wide kernel for the rows handed on.
 template <bool BF16>
-int launch_fast(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStream_t st) {
+int launch_fast(const KArgs &a0, const Scratch &sc, int J, int wide_kcap, cudaStream_t st) {
+  KArgs a = a0;
+  a.approx_c0 = approx_bound_c0(a.V, J);
   constexpr int esz = BF16 ? 2 : 4;
   const int span = ((a.V * esz + 15) / 16) * 16 + 16;
   int stages = BF16 ? 3 : 2;
@@ -1726,7 +1843,7 @@ int launch_fast(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaStr
   const int sel_grid = std::max(1, std::min((a.N + kSelWarps - 1) / kSelWarps, sms * sel_occ));
   sample_select_kernel<<<sel_grid, kSelThreads, 0, st>>>(a, sc.heads, sc.cands);
   if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
-  return launch_wide<BF16>(a, 1, wide_kcap, st);
+  return launch_wide<BF16>(a, 1, wide_kcap, st, 1 << 30, sc.heads, sc.cands);
 }
 
 // Small batches: one CTA per row runs the stats kernel's four warps and then,

@@ -41,6 +41,9 @@ struct KArgs {
   uint32_t *wide_done;
   int64_t deferred_cap;  // entries of `deferred`; hand-offs beyond it flag the row
   int32_t *error;        // set to 1 when a bounded wait gives up
+  // the row-independent part of the approximate full-row sum's relative error
+  // bound (set by the launcher of the approximate-sum kernels)
+  float approx_c0;
 };
 
 // Per-row results the stats kernel passes to the select kernel. The header
@@ -130,8 +133,8 @@ int set_error(int code, const char *msg);
 // Draw u [rows, k] = uniform(key, rows * k) (sample_noise).
 int launch_uniform(uint2 key, int rows, int k, float *u, cudaStream_t stream);
 
-// Debug: y = exp_full(x) (op 0), log_full(x) (op 1), exp_term(x) (op 2), or the
-// per-row-reciprocal quotient x / T (op 3) on device.
+// Debug: y = exp_full(x) (op 0), log_full(x) (op 1), exp_term(x) (op 2), the
+// per-row-reciprocal quotient x / T (op 3) or the SFU's 2^x (op 4) on device.
 int launch_math(int op, const float *x, float *y, int64_t n, float T, cudaStream_t stream);
 
 // Debug: count x in [lo, hi) (float bit patterns, step `step`, within the

@@ -253,16 +253,15 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
   const int k4 = (k + 3) & ~3;
   float *scr_lo = exact ? scr : scr + k4;
   float lsum = 0.0f;
-  for (int r = lane; r < k4; r += 32) {
-    float e = 0.0f, el = 0.0f;
-    if (r < k) {
-      const float v = cand_value(sorted[r]);
-      e = exp_full(__fsub_rn(v, lse_hi));
-      el = exact ? e : exp_full(__fsub_rn(v, lse_lo));
-    }
-    scr[r] = e;
-    if (!exact) scr_lo[r] = el;
-    lsum = __fadd_rn(lsum, el);
+  // slot t < k4: rank t under lse_hi; slot t >= k4 (interval only): rank t - k4
+  // under lse_lo, at scr_lo[t - k4] = scr[t]
+  const int nt = exact ? k4 : 2 * k4;
+  for (int t = lane; t < nt; t += 32) {
+    const bool lo = t >= k4;
+    const int r = lo ? t - k4 : t;
+    const float e = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lo ? lse_lo : lse_hi)) : 0.0f;
+    scr[t] = e;
+    if (lo || exact) lsum = __fadd_rn(lsum, e);
   }
   // Any-order sum of the k terms: a sequential sum of nonnegative terms differs
   // from it by at most 2 (k - 1) 2^-24 relative (< 3.1e-5 for k <= 256). When
@@ -376,13 +375,16 @@ __device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v)
 // 2^-46)) is then bracketed by the same expression at the bracket's ends: RN
 // and log are monotone there (log is checked over every float in [1, 16384) by
 // the tests).
+// Called by a whole warp: lane 0 takes the low end, lane 1 the high end.
 __device__ __forceinline__ void lse_bounds(unsigned long long S, float gmax, float c0,
-                                           float &lse_lo, float &lse_hi) {
+                                           float &lse_lo, float &lse_hi, int lane) {
   const float delta = __fmaf_ru(0x1.8cccccp-23f, fabsf(gmax), c0);
   const float lo = __fmul_rd(__fmul_rd(__ull2float_rd(S), __fsub_rd(1.0f, delta)), 0x1p-46f);
   const float hi = __fmul_ru(__fmul_ru(__ull2float_ru(S), __fadd_ru(1.0f, delta)), 0x1p-46f);
-  lse_lo = __fadd_rn(gmax, log_full(fmaxf(lo, 1.0f)));  // the exact S is at least 2^46
-  lse_hi = __fadd_rn(gmax, log_full(hi));
+  // the exact S is at least 2^46
+  const float lg = log_full(lane == 0 ? fmaxf(lo, 1.0f) : hi);
+  lse_lo = __fadd_rn(gmax, __shfl_sync(kFull, lg, 0));
+  lse_hi = __fadd_rn(gmax, __shfl_sync(kFull, lg, 1));
 }
 
 // Per-row parameters as stored (read one row ahead of use).
@@ -1035,7 +1037,24 @@ __device__ __forceinline__ void stage_row(const RowHead *heads, const RowCands *
 }
 
 // The top k of a row's C <= 256 candidates (the first kStageCands in cs, all of
-// them in Cs), keyed by their exact quotients, in rank order into sk.
+// them in Cs), keyed by their exact quotients in one pass into sk (>= C keys of
+// shared memory) and ranked there in place: sk[0 .. k) in rank order.
+__device__ __forceinline__ void rank_cands_smem(const unsigned long long *cs, const RowCands &Cs,
+                                                int C, int k, float T, unsigned long long *sk,
+                                                int lane) {
+  for (int e = lane; e < C; e += 32) sk[e] = raw_to_key(e < kStageCands ? cs[e] : Cs.cand[e], T);
+  __syncwarp();
+  if (C <= 32)
+    sort_list<1>(sk, C, k, lane);
+  else if (C <= 64)
+    sort_list<2>(sk, C, k, lane);
+  else if (C <= 128)
+    sort_list<4>(sk, C, k, lane);
+  else
+    select_list(sk, C, k, lane);
+}
+
+// The same ranking with the keys in registers (sk needs only k entries).
 __device__ __forceinline__ void rank_cands(const unsigned long long *cs, const RowCands &Cs, int C,
                                            int k, float T, unsigned long long *sk, int lane) {
   if (C <= 32)
@@ -1064,13 +1083,13 @@ __device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHea
   }
   float lse_lo, lse_hi;
   if (H.approx) {
-    lse_bounds(S, H.gmax, a.approx_c0, lse_lo, lse_hi);
+    lse_bounds(S, H.gmax, a.approx_c0, lse_lo, lse_hi, lane);
   } else {
     lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
     lse_hi = lse_lo;
   }
   const uint2 key = raw_key(a, raw, lane);
-  rank_cands(cs, Cs, C, rp.k, rp.T, sk, lane);
+  rank_cands_smem(cs, Cs, C, rp.k, rp.T, sk, lane);
   __syncwarp();
   return sample_tail(a, row, key, sk, scr, rp.k, lse_lo, lse_hi, rp.p, lane);
 }
@@ -1174,7 +1193,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
       for (int i = 0; i < kSelWarps; ++i) Se += exact_red[i];
       const float lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
       const RowCands &Cs = cands[xrow];
-      rank_cands(Cs.cand, Cs, H.cnt, rp.k, rp.T, sk, lane);
+      rank_cands_smem(Cs.cand, Cs, H.cnt, rp.k, rp.T, sk, lane);
       __syncwarp();
       sample_tail(a, xrow, row_key(a, xrow), sk, scr_all[0], rp.k, lse, lse, rp.p, lane);
     }

@@ -615,17 +615,17 @@ __device__ __forceinline__ void stats_row_approx(RowHead &H, RowCands &Cs, unsig
                                                  int t, int lane, int w) {
   const float2 c2 = make_float2(c, c), g2 = make_float2(g, g);
   const float2 tl2 = make_float2(tau_lo, tau_lo), m1 = make_float2(-1.0f, -1.0f);
-  float2 s2 = make_float2(0.0f, 0.0f);
+  float2 s2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};  // even / odd columns
   uint32_t bx = 0u, by = 0u;
 #pragma unroll
   for (int j = JJ - 1; j >= 0; --j) {
     const float2 u = __ffma2_rn(x2[j], c2, g2);
-    s2 = __fadd2_rn(s2, make_float2(ex2_approx(u.x), ex2_approx(u.y)));
+    s2[j & 1] = __fadd2_rn(s2[j & 1], make_float2(ex2_approx(u.x), ex2_approx(u.y)));
     const float2 d = __ffma2_rn(x2[j], m1, tl2);
     bx = __funnelshift_l(__float_as_uint(d.x), bx, 1);
     by = __funnelshift_l(__float_as_uint(d.y), by, 1);
   }
-  stats_finish<BF16>(H, Cs, cand_n, rb, s2, bx, by, gmax, 1, t, lane, w);
+  stats_finish<BF16>(H, Cs, cand_n, rb, __fadd2_rn(s2[0], s2[1]), bx, by, gmax, 1, t, lane, w);
 }
 
 // Rows the approximate stats take: k <= 128 (the tail's scratch holds both
@@ -636,6 +636,20 @@ constexpr int kApproxMaxK = 128;
 __device__ __forceinline__ bool approx_row_ok(const RowP &rp, float xmax, float taux) {
   return rp.k <= kApproxMaxK && rp.T >= 0x1p-17f && rp.T <= 0x1p20f && fabsf(xmax) <= 0x1p60f &&
          fabsf(taux) >= 0x1p-60f;
+}
+
+// A lower bound of the r-th largest of the warp's 32 values (1 <= r <= 32): r
+// rounds of removing every copy of the current maximum (a tie removed at once
+// counts once, which can only lower the result). Every lane at or above the
+// result holds a value at least that large, and at least r lanes do.
+__device__ __forceinline__ float warp_rth_redux(float v, int r) {
+  float m;
+  for (int it = 0;; ++it) {
+    m = warp_max(v);
+    if (it + 1 >= r) break;
+    v = v == m ? -f_inf() : v;
+  }
+  return m;
 }
 
 // The r-th largest of the warp's 32 lane maxima (r <= 32), by a bitonic sort.
@@ -744,7 +758,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       if (pst == D3S_ROW_OK && rp.k <= kFastMaxK && wm == wm) {
         const int r = (rp.k + kFastW - 1) / kFastW;
         if (r <= 32) {
-          tw = warp_rth_of32(lm, r, lane);
+          tw = APPROX ? warp_rth_redux(lm, r) : warp_rth_of32(lm, r, lane);
         } else {
           float v2[PP];
 #pragma unroll

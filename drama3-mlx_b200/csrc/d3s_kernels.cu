@@ -681,7 +681,7 @@ __device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k, f
 // lse, its subkey, the top k of its candidates in rank order in sk, the tail.
 __device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHead &H,
                                            const unsigned long long *cs, const RowCands &Cs,
-                                           const RawP &raw, const RowP &rp,
+                                           uint2 key, const RowP &rp,
                                            unsigned long long *sk, float *scr, int lane);
 
 // APPROX: rows that approx_row_ok accepts take stats_row_approx and are marked
@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       // sorted keys and the tail's scratch.
       __syncthreads();
       if (w == 0 && !H.done)
-        (void)select_row(a, row, H, cands[row].cand, cands[row], cur, rp,
+        (void)select_row(a, row, H, cands[row].cand, cands[row], raw_key(a, cur, lane), rp,
                    reinterpret_cast<unsigned long long *>(dsm),
                    reinterpret_cast<float *>(dsm + kCandCap * 8), lane);
     }
@@ -1081,11 +1081,12 @@ __device__ __forceinline__ void rank_cands(const unsigned long long *cs, const R
     select_cands(Cs, C, k, T, sk, lane);
 }
 
-// Returns false, having written nothing, when the row's top-p cut needs the
-// exact full-row sum (an approximate-sum row whose cut is uncertain).
+// key draws the row's uniforms. Returns false, having written nothing, when
+// the row's top-p cut needs the exact full-row sum (an approximate-sum row
+// whose cut is uncertain).
 __device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHead &H,
                                            const unsigned long long *cs, const RowCands &Cs,
-                                           const RawP &raw, const RowP &rp,
+                                           uint2 key, const RowP &rp,
                                            unsigned long long *sk, float *scr, int lane) {
   const int C = H.cnt;
   unsigned long long S = 0;
@@ -1102,7 +1103,6 @@ __device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHea
     lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
     lse_hi = lse_lo;
   }
-  const uint2 key = raw_key(a, raw, lane);
   rank_cands_smem(cs, Cs, C, rp.k, rp.T, sk, lane);
   __syncwarp();
   return sample_tail(a, row, key, sk, scr, rp.k, lse_lo, lse_hi, rp.p, lane);
@@ -1125,13 +1125,22 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
   int row = gw, b = 0;
   RawP raw;
   int cnt_next = 0;  // candidate count of row + nw
+  // The keys of the warp's next 32 rows, lane i holding that of the i-th: one
+  // key derivation per lane instead of one per row on two lanes.
+  uint2 keys32 = make_uint2(0u, 0u);
   if (row < a.N) {
     stage_row(heads, cands, row, row_count(heads, row), stg_all[w][0], lane);
     raw = load_raw(a, row);
     if (row + nw < a.N) cnt_next = row_count(heads, row + nw);
   }
   cp_async_commit();
-  for (; row < a.N; row += nw, b ^= 1) {
+  for (int iter = 0; row < a.N; row += nw, b ^= 1, ++iter) {
+    if ((iter & 31) == 0) {
+      const int r = row + lane * nw;
+      if (r < a.N) keys32 = row_key(a, r);
+    }
+    const uint2 key = make_uint2(__shfl_sync(kFull, keys32.x, iter & 31),
+                                 __shfl_sync(kFull, keys32.y, iter & 31));
     // the next row's header and candidates are copied while this row is
     // sampled, and the count of the row after it is read
     const int nrow = row + nw;
@@ -1150,7 +1159,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
     if (!st.head.done) {
       RowP rp;
       resolve(a, raw, rp);  // valid: the stats kernel flagged every other row
-      if (!select_row(a, row, st.head, st.cand, cands[row], raw, rp, sk, scr_all[w], lane) &&
+      if (!select_row(a, row, st.head, st.cand, cands[row], key, rp, sk, scr_all[w], lane) &&
           lane == 0) {
         const unsigned pos = atomicAdd(&exact_n, 1u);
         if (pos < (unsigned)kSelExactRows)

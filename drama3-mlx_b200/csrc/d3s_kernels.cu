@@ -361,30 +361,35 @@ __device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v)
   return (unsigned long long)p0 + ((unsigned long long)p1 << 21) + ((unsigned long long)p2 << 42);
 }
 
-// Bounds on the exact lse of a row from its approximate full-row sum S (2^-46
-// fixed point, the SFU's exp2 of RN(x c + g) with c = RN(log2(e) / T) and
-// g = RN(-xmax c)).
-// With G = |max x / T|, first-order error analysis bounds |S_exact - S| / S by
+// The lse bracket of one row from its header, computed by one thread. For a
+// row of the approximate stats, S (2^-46 fixed point) is the SFU's exp2 of
+// RN(x c + g) with c = RN(log2(e) / T) and g = RN(-xmax c). With G = |max x / T|,
+// first-order error analysis bounds |S_exact - S| / S by
 // 2^-24 (3 G + 5 ln V + n_p + L + 1) + e_exp + e_ex2: the quotients' and
 // differences' roundings (2G + 2 ln V for the exact sum, G + 3 ln V for the
 // approximate one, ln V bounding the entropy-weighted |x/T - max|), sequential
 // sums of n_p (the exact partials) and L (the approximate accumulators) terms,
 // exp's relative error (below 2^-23.5) and ex2.approx's (below 2^-22.5; both
-// checked by the tests). approx_bound_c0 rounds the row-independent part up;
-// the row's part is 3.1 G 2^-24. The exact lse = RN(gmax + log(RN(S_exact)
+// checked by the tests). approx_bound_c0 (c0) rounds the row-independent part
+// up; the row's part is 3.1 G 2^-24. The exact lse = RN(gmax + log(RN(S_exact)
 // 2^-46)) is then bracketed by the same expression at the bracket's ends: RN
 // and log are monotone there (log is checked over every float in [1, 16384) by
-// the tests).
-// Called by a whole warp: lane 0 takes the low end, lane 1 the high end.
-__device__ __forceinline__ void lse_bounds(unsigned long long S, float gmax, float c0,
-                                           float &lse_lo, float &lse_hi, int lane) {
-  const float delta = __fmaf_ru(0x1.8cccccp-23f, fabsf(gmax), c0);
-  const float lo = __fmul_rd(__fmul_rd(__ull2float_rd(S), __fsub_rd(1.0f, delta)), 0x1p-46f);
-  const float hi = __fmul_ru(__fmul_ru(__ull2float_ru(S), __fadd_ru(1.0f, delta)), 0x1p-46f);
-  // the exact S is at least 2^46
-  const float lg = log_full(lane == 0 ? fmaxf(lo, 1.0f) : hi);
-  lse_lo = __fadd_rn(gmax, __shfl_sync(kFull, lg, 0));
-  lse_hi = __fadd_rn(gmax, __shfl_sync(kFull, lg, 1));
+// the tests), and the exact S is at least 2^46. Rows of the exact stats get
+// their exact lse twice.
+__device__ __forceinline__ void row_lse(const RowHead &H, float c0, float &lse_lo, float &lse_hi) {
+  unsigned long long S = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) S += H.sum[i];
+  if (H.approx) {
+    const float delta = __fmaf_ru(0x1.8cccccp-23f, fabsf(H.gmax), c0);
+    const float lo = __fmul_rd(__fmul_rd(__ull2float_rd(S), __fsub_rd(1.0f, delta)), 0x1p-46f);
+    const float hi = __fmul_ru(__fmul_ru(__ull2float_ru(S), __fadd_ru(1.0f, delta)), 0x1p-46f);
+    lse_lo = __fadd_rn(H.gmax, log_full(fmaxf(lo, 1.0f)));
+    lse_hi = __fadd_rn(H.gmax, log_full(hi));
+  } else {
+    lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
+    lse_hi = lse_lo;
+  }
 }
 
 // Per-row parameters as stored (read one row ahead of use).
@@ -679,9 +684,9 @@ __device__ __forceinline__ void select_cands(const RowCands &Cs, int C, int k, f
 
 // The select kernel's work on one row whose record is complete: the row's
 // lse, its subkey, the top k of its candidates in rank order in sk, the tail.
-__device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHead &H,
+__device__ __forceinline__ bool select_row(const KArgs &a, int row, int C,
                                            const unsigned long long *cs, const RowCands &Cs,
-                                           uint2 key, const RowP &rp,
+                                           uint2 key, const RowP &rp, float lse_lo, float lse_hi,
                                            unsigned long long *sk, float *scr, int lane);
 
 // APPROX: rows that approx_row_ok accepts take stats_row_approx and are marked
@@ -847,10 +852,13 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       // candidates, warp 0 samples the row; the stage is free and holds the
       // sorted keys and the tail's scratch.
       __syncthreads();
-      if (w == 0 && !H.done)
-        (void)select_row(a, row, H, cands[row].cand, cands[row], raw_key(a, cur, lane), rp,
-                   reinterpret_cast<unsigned long long *>(dsm),
-                   reinterpret_cast<float *>(dsm + kCandCap * 8), lane);
+      if (w == 0 && !H.done) {
+        float lse_lo, lse_hi;
+        row_lse(H, a.approx_c0, lse_lo, lse_hi);
+        (void)select_row(a, row, H.cnt, cands[row].cand, cands[row], raw_key(a, cur, lane), rp,
+                         lse_lo, lse_hi, reinterpret_cast<unsigned long long *>(dsm),
+                         reinterpret_cast<float *>(dsm + kCandCap * 8), lane);
+      }
     }
   }
   if (failed) {
@@ -1081,27 +1089,16 @@ __device__ __forceinline__ void rank_cands(const unsigned long long *cs, const R
     select_cands(Cs, C, k, T, sk, lane);
 }
 
-// key draws the row's uniforms. Returns false, having written nothing, when
-// the row's top-p cut needs the exact full-row sum (an approximate-sum row
-// whose cut is uncertain).
-__device__ __forceinline__ bool select_row(const KArgs &a, int row, const RowHead &H,
+// key draws the row's uniforms; the row's lse lies in [lse_lo, lse_hi] (equal
+// when exact). Returns false, having written nothing, when the row's top-p cut
+// needs the exact full-row sum (an approximate-sum row whose cut is uncertain).
+__device__ __forceinline__ bool select_row(const KArgs &a, int row, int C,
                                            const unsigned long long *cs, const RowCands &Cs,
-                                           uint2 key, const RowP &rp,
+                                           uint2 key, const RowP &rp, float lse_lo, float lse_hi,
                                            unsigned long long *sk, float *scr, int lane) {
-  const int C = H.cnt;
-  unsigned long long S = 0;
-#pragma unroll
-  for (int i = 0; i < kFastW; ++i) S += H.sum[i];
   if (C > kCandCap) {  // more candidates than the list holds (ties): the wide kernel's exact path
     if (lane == 0) defer_row(a, row);
     return true;
-  }
-  float lse_lo, lse_hi;
-  if (H.approx) {
-    lse_bounds(S, H.gmax, a.approx_c0, lse_lo, lse_hi, lane);
-  } else {
-    lse_lo = __fadd_rn(H.gmax, log_full(__fmul_rn(__ull2float_rn(S), 0x1p-46f)));
-    lse_hi = lse_lo;
   }
   rank_cands_smem(cs, Cs, C, rp.k, rp.T, sk, lane);
   __syncwarp();
@@ -1123,33 +1120,45 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
   const int gw = blockIdx.x * kSelWarps + w, nw = gridDim.x * kSelWarps;
   unsigned long long *sk = sk_all[w];
   int row = gw, b = 0;
-  RawP raw;
   int cnt_next = 0;  // candidate count of row + nw
-  // The keys of the warp's next 32 rows, lane i holding that of the i-th: one
-  // key derivation per lane instead of one per row on two lanes.
-  uint2 keys32 = make_uint2(0u, 0u);
+  // The per-row scalars of the warp's next 32 rows, lane i holding those of
+  // the i-th (its key, its lse bracket from the header, its parameters): one
+  // key derivation and one pair of logs per lane instead of per row.
+  uint2 key32 = make_uint2(0u, 0u);
+  float lo32 = 0.0f, hi32 = 0.0f, T32 = 1.0f, p32 = 1.0f;
+  int k32 = 1;
   if (row < a.N) {
     stage_row(heads, cands, row, row_count(heads, row), stg_all[w][0], lane);
-    raw = load_raw(a, row);
     if (row + nw < a.N) cnt_next = row_count(heads, row + nw);
   }
   cp_async_commit();
   for (int iter = 0; row < a.N; row += nw, b ^= 1, ++iter) {
     if ((iter & 31) == 0) {
       const int r = row + lane * nw;
-      if (r < a.N) keys32 = row_key(a, r);
+      if (r < a.N && !heads[r].done) {
+        key32 = row_key(a, r);
+        row_lse(heads[r], a.approx_c0, lo32, hi32);
+        RowP rr;
+        resolve(a, load_raw(a, r), rr);  // valid: the stats kernel flagged every other row
+        T32 = rr.T;
+        p32 = rr.p;
+        k32 = rr.k;
+      }
     }
-    const uint2 key = make_uint2(__shfl_sync(kFull, keys32.x, iter & 31),
-                                 __shfl_sync(kFull, keys32.y, iter & 31));
+    const int src = iter & 31;
+    const uint2 key = make_uint2(__shfl_sync(kFull, key32.x, src), __shfl_sync(kFull, key32.y, src));
+    const float lse_lo = __shfl_sync(kFull, lo32, src), lse_hi = __shfl_sync(kFull, hi32, src);
+    RowP rp;
+    rp.T = __shfl_sync(kFull, T32, src);
+    rp.p = __shfl_sync(kFull, p32, src);
+    rp.k = __shfl_sync(kFull, k32, src);
     // the next row's header and candidates are copied while this row is
     // sampled, and the count of the row after it is read
     const int nrow = row + nw;
-    RawP rawn;
     int cnt_nn = 0;
     __syncwarp();
     if (nrow < a.N) {
       stage_row(heads, cands, nrow, cnt_next, stg_all[w][b ^ 1], lane);
-      rawn = load_raw(a, nrow);
       if (nrow + nw < a.N) cnt_nn = row_count(heads, nrow + nw);
     }
     cp_async_commit();
@@ -1157,9 +1166,8 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
     __syncwarp();
     const SelStage &st = stg_all[w][b];
     if (!st.head.done) {
-      RowP rp;
-      resolve(a, raw, rp);  // valid: the stats kernel flagged every other row
-      if (!select_row(a, row, st.head, st.cand, cands[row], key, rp, sk, scr_all[w], lane) &&
+      if (!select_row(a, row, st.head.cnt, st.cand, cands[row], key, rp, lse_lo, lse_hi, sk,
+                      scr_all[w], lane) &&
           lane == 0) {
         const unsigned pos = atomicAdd(&exact_n, 1u);
         if (pos < (unsigned)kSelExactRows)
@@ -1168,7 +1176,6 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
           defer_row_exact_sum(a, row);
       }
     }
-    raw = rawn;
     cnt_next = cnt_nn;
   }
   // The rows whose cut needed the exact full-row sum, by the whole CTA once its
@@ -1852,7 +1859,7 @@ int launch_wide(const KArgs &a, int use_list, int kcap, cudaStream_t st, int max
 }
 
 // The row-independent part of the approximate full-row sum's error bound (see
-// lse_bounds) for rows of V with J columns per stats thread, rounded up:
+// row_lse) for rows of V with J columns per stats thread, rounded up:
 // 2^-24 (1.01 (5 ln V + n_p + L + 1 + 6) + 1), where n_p = ceil(V / 256) and
 // L = J terms per accumulator.
 float approx_bound_c0(int V, int J) {

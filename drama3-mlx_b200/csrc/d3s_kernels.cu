@@ -717,17 +717,41 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       const int r = blockIdx.x + s * gridDim.x;
       if (r < a.N) issue_row<ESZ>(a, r, dsm + (size_t)s * span, &sm.mbar[s], pol);
     }
-  RawP nxt;
-  if ((int)blockIdx.x < a.N) nxt = load_raw(a, blockIdx.x);
+  RawP nxt{};
+  if (SELECT && (int)blockIdx.x < a.N) nxt = load_raw(a, blockIdx.x);
+  // Persistent CTAs: each warp resolves the parameters of the CTA's next 32
+  // rows at once, lane i those of the i-th, and shuffles them out per row.
+  float T32 = 1.0f, p32 = 1.0f;
+  int k32 = 1, st32 = D3S_ROW_BADPARAM;
   int it = 0;
   bool failed = false;
   for (;; ++it) {
     const int row = blockIdx.x + it * gridDim.x;
     if (row >= a.N) break;
-    const RawP cur = nxt;
-    if (row + (int)gridDim.x < a.N) nxt = load_raw(a, row + gridDim.x);
     RowP rp;
-    const int pst = resolve(a, cur, rp);
+    int pst;
+    RawP cur{};
+    if constexpr (SELECT) {
+      cur = nxt;
+      if (row + (int)gridDim.x < a.N) nxt = load_raw(a, row + gridDim.x);
+      pst = resolve(a, cur, rp);
+    } else {
+      if ((it & 31) == 0) {
+        const int r = row + lane * (int)gridDim.x;
+        if (r < a.N) {
+          RowP q{1.0f, 1.0f, 1};
+          st32 = resolve(a, load_raw(a, r), q);
+          T32 = q.T;
+          p32 = q.p;
+          k32 = q.k;
+        }
+      }
+      const int src = it & 31;
+      pst = __shfl_sync(kFull, st32, src);
+      rp.T = __shfl_sync(kFull, T32, src);
+      rp.p = __shfl_sync(kFull, p32, src);
+      rp.k = __shfl_sync(kFull, k32, src);
+    }
     const int s = it % stages, par = it & 1;
     const bool ok = mbar_wait_bounded(&sm.mbar[s], (uint32_t)(it / stages) & 1u);
     const unsigned char *rb =

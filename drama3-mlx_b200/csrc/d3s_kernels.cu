@@ -721,7 +721,8 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
   if (SELECT && (int)blockIdx.x < a.N) nxt = load_raw(a, blockIdx.x);
   // Persistent CTAs: each warp resolves the parameters of the CTA's next 32
   // rows at once, lane i those of the i-th, and shuffles them out per row.
-  float T32 = 1.0f, p32 = 1.0f;
+  // (approximate kernels also take each row's RN(log2(e) / T) and RN(1 / T))
+  float T32 = 1.0f, p32 = 1.0f, c32 = 1.0f, rT32 = 1.0f;
   int k32 = 1, st32 = D3S_ROW_BADPARAM;
   int it = 0;
   bool failed = false;
@@ -744,6 +745,10 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
           T32 = q.T;
           p32 = q.p;
           k32 = q.k;
+          if constexpr (APPROX) {
+            c32 = __fdiv_rn(kL2E, q.T);
+            rT32 = __frcp_rn(q.T);
+          }
         }
       }
       const int src = it & 31;
@@ -823,15 +828,31 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
         xmin = fminf(xmin, sm.red_min[par][i]);
         taux = fminf(taux, sm.red_tau[par][i]);
       }
-      // the row's four quotients in one divide across lanes: max (max(x / T) =
-      // RN(max(x) / T), RN being monotone), threshold, min (APPROX: log2(e) / T),
-      // and 1 / T (= RN(1 / T))
-      const float num = lane == 0 ? xmax : (lane == 1 ? taux : (lane == 2 ? (APPROX ? kL2E : xmin) : 1.0f));
-      const float quo = __fdiv_rn(num, rp.T);
-      const float gmax = __shfl_sync(kFull, quo, 0);
-      const float tau = __shfl_sync(kFull, quo, 1);
-      const float q2nd = __shfl_sync(kFull, quo, 2);
-      const float rT = __shfl_sync(kFull, quo, 3);
+      float gmax, tau, q2nd, rT;
+      if constexpr (APPROX && !SELECT) {
+        // log2(e) / T and 1 / T from the 32-row batch; max / T (= max(x / T), RN
+        // being monotone) by the per-row reciprocal where that is the IEEE
+        // quotient; the threshold's quotient only for rows of the exact path
+        const int src = it & 31;
+        q2nd = __shfl_sync(kFull, c32, src);
+        rT = __shfl_sync(kFull, rT32, src);
+        const float ax = fabsf(xmax);
+        gmax = (ax >= 0x1p-100f && ax <= 0x1p60f && rp.T >= 0x1p-17f && rp.T <= 0x1p20f)
+                   ? div_rows(xmax, rT, -rp.T)
+                   : __fdiv_rn(xmax, rp.T);
+        tau = 0.0f;
+      } else {
+        // the row's four quotients in one divide across lanes: max (max(x / T) =
+        // RN(max(x) / T), RN being monotone), threshold, min (APPROX: log2(e) /
+        // T), and 1 / T (= RN(1 / T))
+        const float num =
+            lane == 0 ? xmax : (lane == 1 ? taux : (lane == 2 ? (APPROX ? kL2E : xmin) : 1.0f));
+        const float quo = __fdiv_rn(num, rp.T);
+        gmax = __shfl_sync(kFull, quo, 0);
+        tau = __shfl_sync(kFull, quo, 1);
+        q2nd = __shfl_sync(kFull, quo, 2);
+        rT = __shfl_sync(kFull, quo, 3);
+      }
       if (!(fabsf(gmax) < f_inf())) {
         if (t == 0) {  // NaN, +inf, or every value -inf
           flag_row(a, row, D3S_ROW_NONFINITE);
@@ -842,8 +863,8 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
                                    __fmul_rn(-xmax, q2nd),
                                    __fmaf_rn(-fabsf(taux), 0x1p-21f, taux), gmax, t, lane, w);
       } else if (APPROX) {  // no row min here: the IEEE divide per element and the term floor
-        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q2, rp.T, rT, gmax, tau,
-                                   -f_inf(), false, t, lane, w);
+        stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q2, rp.T, rT, gmax,
+                                   __fdiv_rn(taux, rp.T), -f_inf(), false, t, lane, w);
       } else {
         stats_row<JJ, BF16, EXACT>(a, H, cands[row], &sm.cand_n[s], rb, q2, rp.T, rT, gmax, tau,
                                    q2nd, div_rows_ok(xmin, xmax, rp.T, gmax, tau), t, lane, w);

@@ -253,15 +253,12 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
   const int k4 = (k + 3) & ~3;
   float *scr_lo = exact ? scr : scr + k4;
   float lsum = 0.0f;
-  // slot t < k4: rank t under lse_hi; slot t >= k4 (interval only): rank t - k4
-  // under lse_lo, at scr_lo[t - k4] = scr[t]
-  const int nt = exact ? k4 : 2 * k4;
-  for (int t = lane; t < nt; t += 32) {
-    const bool lo = t >= k4;
-    const int r = lo ? t - k4 : t;
-    const float e = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lo ? lse_lo : lse_hi)) : 0.0f;
-    scr[t] = e;
-    if (lo || exact) lsum = __fadd_rn(lsum, e);
+  // the terms under lse_lo first (exact: the only terms); those under lse_hi
+  // are needed only when the sum below leaves a cut possible
+  for (int r = lane; r < k4; r += 32) {
+    const float e = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lse_lo)) : 0.0f;
+    scr_lo[r] = e;
+    lsum = __fadd_rn(lsum, e);
   }
   // Any-order sum of the k terms: a sequential sum of nonnegative terms differs
   // from it by at most 2 (k - 1) 2^-24 relative (< 3.1e-5 for k <= 256). When
@@ -272,6 +269,11 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
   __syncwarp();
   int kept = k;
   if (!(__fmul_rn(lsum, 1.0001f) <= top_p)) {
+    if (!exact) {
+      for (int r = lane; r < k4; r += 32)
+        scr[r] = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lse_hi)) : 0.0f;
+      __syncwarp();
+    }
     // cum_r = e_0 + ... + e_r in rank order; the first r > 0 with cum_r > top_p
     // is the cut. Four ranks per step: the running sums, then one test.
     // Under an interval the same running sums of the terms under lse_lo go

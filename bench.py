@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip configs 2-4 in the default line (rank 0, one GPU)")
     ap.add_argument("--workload", choices=["c5", "c3", "c4"], default="c5",
                     help="c5: the headline line; c3 (lm_head + sample) and c4 (tower frames) "
                          "print their own lines for the design notes")
@@ -92,8 +94,8 @@ class Clocks:
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
                0x4: "sw_power_cap"}
 
-    def __init__(self, uuid: str | None, index: int = 0):
-        self.uuid, self.index = uuid, index
+    def __init__(self, uuid: str | None, index: int = 0, interval_s: float = 0.001):
+        self.uuid, self.index, self.interval_s = uuid, index, interval_s
         self.samples = []
         self.max_mhz = None
         self.err = None
@@ -130,7 +132,7 @@ class Clocks:
                                          int(get_reasons(h))))
                 except Exception:
                     pass
-                self._stop.wait(0.001)
+                self._stop.wait(self.interval_s)
 
         self._thread = threading.Thread(target=poll, daemon=True)
         self._thread.start()
@@ -149,7 +151,19 @@ class Clocks:
         sm = [c for c, _ in self.samples]
         reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items() if r & bit})
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(self.samples), "source": "NVML, ~1 ms polling during the timed region"}
+                "samples": len(self.samples),
+                "source": f"NVML, ~{self.interval_s * 1e3:g} ms polling during the timed region"}
+
+
+def merge_clocks(per_rank: list[dict]) -> dict:
+    """One clocks record for the job: the lowest per-rank median SM clock, the
+    union of the throttle reasons seen on any rank, and each rank's record."""
+    mhz = [c["sm_mhz"] for c in per_rank if c.get("sm_mhz") is not None]
+    reasons = sorted({r for c in per_rank for r in c.get("reasons", [])})
+    return {"sm_mhz": min(mhz) if mhz else None,
+            "sm_max_mhz": next((c["sm_max_mhz"] for c in per_rank if c.get("sm_max_mhz")), None),
+            "reasons": reasons, "per_rank": per_rank,
+            "source": "NVML on every rank during the timed region; sm_mhz = lowest rank median"}
 
 
 def cpu_baseline(x_host, T, p, k, seeds, target_s: float = 8.0):
@@ -178,7 +192,8 @@ def host_workload(rows: int, seed: int):
     """Config-5 rows on the host (numpy) for the CPU arm."""
     import numpy as np
     rng = np.random.default_rng(seed)
-    x = (rng.standard_normal((rows, V), dtype=np.float32) * 3.0).astype(np.float32)
+    x = rng.standard_normal((rows, V), dtype=np.float32)
+    x *= np.float32(3.0)
     T = rng.uniform(0.5, 1.2, rows).astype(np.float32)
     p = rng.uniform(0.5, 1.0, rows).astype(np.float32)
     k = rng.integers(1, 65, rows).astype(np.int32)
@@ -187,6 +202,11 @@ def host_workload(rows: int, seed: int):
 
 
 def run_reference(args):
+    """The reference arm: the reference's algorithm for this path timed on the
+    host cores. src/sampling.c needs mlx-c, which cannot be built here, so the
+    timed implementation is its C restatement (oracle/d3s_oracle.c, OpenMP over
+    rows, every host thread); each step samples a bounded slice of the same
+    65536-row config-5 batch the GPU arm samples."""
     rank, world, _ = env_ranks()
     if rank != 0:
         return
@@ -195,26 +215,29 @@ def run_reference(args):
     import oracle
     cores = os.cpu_count() or 1
     oracle.lib()
-    x, T, p, k, seeds = host_workload(32768, 7)
+    x, T, p, k, seeds = host_workload(args.rows, 7)
     t0 = time.perf_counter()
     oracle.sample_rows(x[:512], T[:512], p[:512], k[:512], seeds[:512], nthreads=cores)
     rate = 512 / (time.perf_counter() - t0)
     per_step = int(min(len(x), max(256, rate * 1.5)))  # about 1.5 s of CPU work per step
-    for _ in range(args.warmup):
-        oracle.sample_rows(x[:per_step], T[:per_step], p[:per_step], k[:per_step], seeds[:per_step],
-                           nthreads=cores)
+    offs = [(i * per_step) % max(1, len(x) - per_step + 1) for i in range(args.warmup + args.steps)]
+    for o in offs[:args.warmup]:
+        oracle.sample_rows(x[o:o + per_step], T[o:o + per_step], p[o:o + per_step],
+                           k[o:o + per_step], seeds[o:o + per_step], nthreads=cores)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.sample_rows(x[:per_step], T[:per_step], p[:per_step], k[:per_step], seeds[:per_step],
-                           nthreads=cores)
+    for o in offs[args.warmup:]:
+        oracle.sample_rows(x[o:o + per_step], T[o:o + per_step], p[o:o + per_step],
+                           k[o:o + per_step], seeds[o:o + per_step], nthreads=cores)
     dt = time.perf_counter() - t0
     value = per_step * args.steps / dt
-    sample = f"{per_step} config-5 rows per step (of the 65536-row batch), oracle port, {cores} threads"
+    sample = (f"{per_step} rows per step, consecutive slices of the same {args.rows}-row config-5 "
+              f"batch, oracle port, {cores} threads")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "rows_per_step": per_step, "V": V},
+            "config": {"workload": WORKLOAD, "rows_per_gpu": args.rows, "rows_per_step": per_step,
+                       "V": V},
             "cpu_baseline": {"value": value, "unit": "rows/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -222,9 +245,32 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def cpu_one_thread_row_us(x_host, T, p, k, seeds, n: int = 2000):
+    """Config 1's CPU reference: the oracle on one host thread, one row per
+    call (p50 of single-row calls) and per row over a run of n rows."""
+    import oracle
+    oracle.lib()
+    per_call = []
+    for i in range(min(n, len(x_host), 400)):
+        t0 = time.perf_counter()
+        oracle.sample_rows(x_host[i:i + 1], T, p, k, seeds + i, nthreads=1)
+        per_call.append((time.perf_counter() - t0) * 1e6)
+    t0 = time.perf_counter()
+    oracle.sample_rows(x_host[:n], T, p, k, seeds, nthreads=1)
+    mean = (time.perf_counter() - t0) * 1e6 / min(n, len(x_host))
+    per_call.sort()
+    return {"c1_cpu_1thread_p50_us": per_call[len(per_call) // 2],
+            "c1_cpu_1thread_mean_us_per_row": mean,
+            "c1_cpu_note": "oracle/d3s_oracle.c (the C restatement of src/sampling.c), 1 thread; "
+                           "p50 of single-row calls through ctypes, mean over a 2000-row run"}
+
+
 def c1_latency(ctx, torch):
-    """Config 1: one [1, 4097] f32 row per call, the global-key path. p50 of the
-    device time per call (events) and of the host-buffer d3_sample call."""
+    """Config 1: one [1, 4097] f32 row per call on the global key. The device
+    time of one call without host submission (a CUDA graph of 100 calls,
+    replayed), events around single Python calls (host submission included),
+    the host-buffer d3_sample call (host in, host out), and the CPU oracle on
+    one thread."""
     import numpy as np
 
     import d3s
@@ -242,16 +288,191 @@ def c1_latency(ctx, torch):
         b.record(st)
     torch.cuda.synchronize()
     dev = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
+    # 100 calls captured once (keys frozen at capture) and replayed: the GPU
+    # time of a call with no host work in between
+    gs = torch.cuda.Stream()
+    gs.wait_stream(st)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(gs):
+        with torch.cuda.graph(graph, stream=gs):
+            for _ in range(100):
+                ctx.sample_top_k_top_p(x, 0.7, 30, 0.7, None, ids, stream=gs)
+    torch.cuda.synchronize()
+    graph_ms = _events_ms(torch, graph.replay, 20)
+    del graph
     h = synth.to_host_logits(synth.c1_rows(1, seed=43))
     walls = []
-    for i in range(520):
+    for i in range(1020):
         t0 = time.perf_counter()
         d3s.sample(h, 0.7, 30, 0.7, i)
         walls.append((time.perf_counter() - t0) * 1e6)
     walls = sorted(walls[20:])
-    return {"c1_device_p50_us": dev[len(dev) // 2], "c1_device_p99_us": dev[int(len(dev) * 0.99)],
-            "c1_host_d3_sample_p50_us": walls[len(walls) // 2],
-            "c1_host_d3_sample_p99_us": walls[int(len(walls) * 0.99)]}
+    out = {"c1_device_graph_us_per_call": graph_ms * 1e3 / 100,
+           "c1_device_p50_us": dev[len(dev) // 2], "c1_device_p99_us": dev[int(len(dev) * 0.99)],
+           "c1_host_d3_sample_p50_us": walls[len(walls) // 2],
+           "c1_host_d3_sample_p99_us": walls[int(len(walls) * 0.99)],
+           "note": "device_graph: 100 calls in one CUDA graph; device_p50: events around one Python "
+                   "call (host submission included); host_d3_sample: d3_sample, host logits in, "
+                   "host id out, wall clock"}
+    xs = synth.to_host_logits(synth.c1_rows(2000, seed=44))
+    out.update(cpu_one_thread_row_us(xs, np.float32(0.7), np.float32(0.7), np.int32(30),
+                                     np.uint64(42)))
+    return out
+
+
+def measure_c2(ctx, torch, iters: int = 1000):
+    """Config 2: bf16 [256, 4097] batches, per-row seeds, T 0.7 / top_p 0.7 /
+    top_k 30, `iters` iterations over 64 distinct batches (134 MB, above L2)."""
+    import synth
+    N = 256
+    xs = [synth.c2_logits(N, seed=500 + i) for i in range(64)]
+    seeds = torch.arange(N, dtype=torch.int64, device="cuda") + 77
+    ids = torch.empty(N, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def one(i):
+        ctx.sample_rows(xs[i % 64], ids, temperature=0.7, top_p=0.7, top_k=30, seeds=seeds)
+
+    for i in range(10):
+        one(i)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(iters)]
+    a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(st)
+    for i, (a, b) in enumerate(evs):
+        a.record(st)
+        one(i)
+        b.record(st)
+    b0.record(st)
+    torch.cuda.synchronize()
+    per = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
+    total_ms = a0.elapsed_time(b0)
+    peak, kind = load_peaks()
+    bytes_batch = N * (2 * V + 8 + 4)
+    p50 = per[len(per) // 2]
+    ctx.check()
+    return {"rows_per_s": N * iters / (total_ms / 1e3), "batch_p50_us": p50,
+            "batch_p99_us": per[int(len(per) * 0.99)],
+            "roofline": {"bound": "hbm", "achieved": bytes_batch / (p50 * 1e-6) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": bytes_batch / (p50 * 1e-6) / 1e9 / peak,
+                         "peak_source": kind, "bytes_per_batch": bytes_batch},
+            "iterations": iters, "kernel": "one CTA per row, select in the same launch + wide (empty)",
+            "note": "a batch is 2.1 MB: latency-bound (launch + one row per CTA), far under HBM"}
+
+
+def measure_c3(ctx, torch, B: int, steps: int, warmup: int):
+    """Config 3 at batch B: the lm_head projection alone (weight re-read from
+    HBM: an L2-clearing read between launches) and the fused projection +
+    sample call."""
+    import d3s
+    import synth
+    D = 2048
+    ctx.reserve(max(B, 1024))
+    h, W = synth.c3_inputs(B, seed=7)
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device="cuda")
+    ids = torch.empty(B, dtype=torch.int32, device="cuda")
+    seeds = torch.arange(B, dtype=torch.int64, device="cuda")
+    # the weight (16.8 MB) fits in L2: a 256 MB read between launches leaves
+    # clean lines (a written buffer's write-back would compete with the reads)
+    flush_buf = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    flush_out = torch.empty((), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def timed(fn):
+        evs = []
+        for i in range(warmup + steps):
+            torch.sum(flush_buf, dim=0, out=flush_out)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            if i >= warmup:
+                evs.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    proj_ms = timed(lambda: ctx.lmhead(h, W, out=logits))
+    fused_ms = timed(lambda: ctx.lmhead_sample(h, W, logits, ids, temperature=0.7, top_p=0.7,
+                                               top_k=30, noise=d3s.NOISE_SEEDS, seeds=seeds))
+    ctx.check()
+    peak_gbs, gkind = load_peaks()
+    peak_tf, tkind = load_tflops()
+    bytes_ = V * D * 2 + B * D * 2 + B * V * 2
+    flops = 2.0 * B * V * D
+    gbs = bytes_ / (proj_ms / 1e3) / 1e9
+    tfs = flops / (proj_ms / 1e3) / 1e12
+    tensor = B > 64
+    del flush_buf
+    return {
+        "B": B, "projection_us": proj_ms * 1e3, "fused_us": fused_ms * 1e3,
+        "fused_rows_per_s": B / (fused_ms / 1e3),
+        "projection_kernel": ("lmhead_gemv_kernel" if B <= 8 else
+                              "lmhead_gemm2_kernel (tcgen05 cta_group::2)" if B >= 512 else
+                              "lmhead_gemm_kernel (tcgen05, split-K)"),
+        "roofline": ({"bound": "tensor", "achieved": tfs, "peak": peak_tf, "unit": "TFLOP/s",
+                      "frac": tfs / peak_tf, "peak_source": tkind + " bf16 burst"} if tensor else
+                     {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s",
+                      "frac": gbs / peak_gbs, "peak_source": gkind}),
+        "hbm_gbs": gbs, "tflops": tfs, "bytes": bytes_, "flops": flops,
+    }
+
+
+def measure_c4(ctx, torch, frames: int):
+    """Config 4: 512 streams x 9 codebook heads per frame (bf16 [512, 1024]
+    rows, Zipf-biased), T 1.0, top_p 0.9, top_k 30, per-stream keys advanced in
+    tower_decode_step order; each frame also draws main + retry on a
+    [512, 4097] backbone row. Heads alone, the whole frame, and the frame
+    replayed from one CUDA graph."""
+    import synth
+    S, H, Vh = 512, 9, 1024
+    ctx.reserve(2 * S)
+    bias = synth.zipf_bias(Vh, 11)
+    heads = [synth.c4_logits(S, seed=100 + j, V=Vh, bias=bias) for j in range(H)]
+    xb = synth.c1_rows(S, seed=5).to(torch.bfloat16)
+    states = torch.randint(0, 2**31 - 1, (S, 2), dtype=torch.int32, device="cuda")
+    hist = torch.zeros(S, 16, dtype=torch.int32, device="cuda")
+    hl = torch.zeros(S, dtype=torch.int32, device="cuda")
+    sub = torch.empty(S, 2 + H, 2, dtype=torch.int32, device="cuda")
+    ids = torch.empty(S, dtype=torch.int32, device="cuda")
+
+    def frame_on(stream=None):
+        ctx.keys_next(states, 2 + H, sub=sub, stream=stream)
+        ctx.frame_main(xb, sub, hist, hl, temperature=1.0, top_p=0.9, top_k=30,
+                       semantic_start=1000, code_vocab=4096, eos_id=7, stream=stream)
+        for j in range(H):
+            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9,
+                                 top_k=30, stream=stream)
+
+    def heads_only():
+        for j in range(H):
+            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9, top_k=30)
+
+    frames = max(1, frames)
+    frame_ms = _events_ms(torch, frame_on, frames)
+    heads_ms = _events_ms(torch, heads_only, frames)
+    ctx.check()
+    gs = torch.cuda.Stream()
+    gs.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(gs):
+        with torch.cuda.graph(graph, stream=gs):
+            frame_on(gs)
+    torch.cuda.synchronize()
+    graph_ms = _events_ms(torch, graph.replay, frames)
+    del graph
+    ctx.check()
+    peak, kind = load_peaks()
+    head_bytes = H * S * (2 * Vh + 4)
+    return {
+        "head_rows_per_s": S * H / (heads_ms / 1e3), "ms_per_frame_heads": heads_ms,
+        "ms_per_frame_all": frame_ms, "frame_rows_per_s": S * (H + 2) / (frame_ms / 1e3),
+        "ms_per_frame_graph": graph_ms, "frame_rows_per_s_graph": S * (H + 2) / (graph_ms / 1e3),
+        "frames": frames,
+        "roofline": {"bound": "hbm", "achieved": head_bytes / (heads_ms / 1e3) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": head_bytes / (heads_ms / 1e3) / 1e9 / peak,
+                     "peak_source": kind, "bytes_per_frame_heads": head_bytes},
+        "note": "a head launch is 512 rows of 2 KB: launch-bound; the frame's rows stay in L2",
+    }
 
 
 def run_ours(args):
@@ -272,58 +493,88 @@ def run_ours(args):
     x, T, p, k, seeds = synth.c5_batch(rows, seed=1000 + rank)
     ids = torch.empty(rows, dtype=torch.int32, device="cuda")
     st = torch.cuda.current_stream()
+    # N > 1: each rank's sampler writes its ids straight into rank 0's result
+    # over NVLink (d3s_gather); the step is complete on rank 0 once every
+    # rank's completion count has landed
+    gather = d3s.Gather(local, world, rank, world * rows, shard.handle_exchange()) \
+        if world > 1 else None
+    gather_out = torch.empty(world * rows, dtype=torch.int32, device="cuda") \
+        if gather is not None and rank == 0 else None
+    step_no = [0]
 
-    def sample():
-        ctx.sample_rows(x, ids, temperature=T, top_p=p, top_k=k, seeds=seeds)
+    def target():
+        """Where this step's ids go: the local tensor, or (N > 1) this rank's
+        rows of rank 0's result (waits until rank 0 released step - 2)."""
+        return gather.begin(step_no[0]) if gather is not None else ids
 
-    def collect():  # the sampled ids of every rank to rank 0 (drama3-mlx_b200/shard.py)
-        if world > 1:
-            shard.gather_ids(ids, world * rows, world, rank)
+    def sample(out):
+        ctx.sample_rows(x, out, temperature=T, top_p=p, top_k=k, seeds=seeds)
+
+    def collect():
+        if gather is None:
+            return
+        gather.end(step_no[0])
+        gather.release(step_no[0])
+        step_no[0] += 1
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
-    def max_over_ranks(v: float) -> float:
+    def over_ranks(vals: list[float]) -> list[list[float]]:
         if world == 1:
-            return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+            return [vals]
+        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [o.tolist() for o in out]
 
+    barrier()
     for _ in range(args.warmup):
-        sample()
+        sample(target())
         collect()
     barrier()
     uuid = str(getattr(torch.cuda.get_device_properties(local), "uuid", "") or "")
     phys = int((os.environ.get("CUDA_VISIBLE_DEVICES", "") or str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else local
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    with Clocks(uuid, phys) as clk:
+    kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
+    with Clocks(uuid, phys, 0.001 if rank == 0 else 0.002) as clk:
         start.record(st)
         for i in range(args.steps):
+            out = target()
             kev[i][0].record(st)
-            sample()
+            sample(out)
             kev[i][1].record(st)
             collect()
+            kev[i][2].record(st)
         end.record(st)
         barrier()
-    elapsed_ms = max_over_ranks(start.elapsed_time(end))
-    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
-    kernel_ms_max = max_over_ranks(kernel_ms)
+    elapsed_local = start.elapsed_time(end)
+    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
+    collect_ms = statistics.mean(b.elapsed_time(c) for _, b, c in kev)
+    per_rank = over_ranks([elapsed_local, kernel_ms, collect_ms])
+    elapsed_ms = max(r[0] for r in per_rank)
+    kernel_ms_max = max(r[1] for r in per_rank)
+    if gather is not None:
+        gather.check()
+    ctx.check()
     clocks = clk.summary()
+    if world > 1:
+        all_clocks = [None] * world
+        dist.all_gather_object(all_clocks, clocks)
+        clocks = merge_clocks(all_clocks)
 
     # end to end through the C ABI with host buffers: pinned host -> device copy of
-    # the step's inputs, the sampler, device -> host copy of the ids, every step
+    # the step's inputs, the sampler, the ids to rank 0 (N > 1), device -> host
+    # copy of the ids, every step
     e2e = None
     if not args.no_e2e:
         hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
         hx.copy_(x)
         hT, hp, hk, hs = (t.cpu().pin_memory() for t in (T, p, k, seeds))
-        hids = torch.empty(rows, dtype=torch.int32, pin_memory=True)
+        hids = torch.empty(world * rows if rank == 0 else rows, dtype=torch.int32, pin_memory=True)
         dx, dT, dp, dk, ds = (torch.empty_like(t) for t in (x, T, p, k, seeds))
         did = torch.empty_like(ids)
 
@@ -333,10 +584,18 @@ def run_ours(args):
             dp.copy_(hp, non_blocking=True)
             dk.copy_(hk, non_blocking=True)
             ds.copy_(hs, non_blocking=True)
-            ctx.sample_rows(dx, did, temperature=dT, top_p=dp, top_k=dk, seeds=ds)
-            hids.copy_(did, non_blocking=True)
-            if world > 1:
-                shard.gather_ids(did, world * rows, world, rank)
+            if gather is None:
+                ctx.sample_rows(dx, did, temperature=dT, top_p=dp, top_k=dk, seeds=ds)
+                hids.copy_(did, non_blocking=True)
+                return
+            s_ = step_no[0]
+            ctx.sample_rows(dx, gather.begin(s_), temperature=dT, top_p=dp, top_k=dk, seeds=ds)
+            gather.end(s_)
+            if rank == 0:
+                gather.copy_result(s_, gather_out)
+                hids.copy_(gather_out, non_blocking=True)
+            gather.release(s_)
+            step_no[0] += 1
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):
@@ -348,20 +607,28 @@ def run_ours(args):
             e2e_step()
         b.record(st)
         barrier()
-        e2e_ms = max_over_ranks(a.elapsed_time(b))
+        e2e_ms = max(r[0] for r in over_ranks([a.elapsed_time(b)]))
+        if gather is not None:
+            gather.check()
         h2d = hx.numel() * hx.element_size() + sum(t.numel() * t.element_size() for t in (hT, hp, hk, hs))
         e2e = {"value": world * rows * e2e_steps / (e2e_ms / 1e3), "unit": "rows/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(rows * 4),
-               "steps": e2e_steps, "path": "pinned host -> cudaMemcpyAsync -> d3s_sample -> ids to host"}
-        if world > 1:
-            e2e["d2h_bytes_per_step"] = int(rows * 4)
+               "h2d_bytes_per_step": int(h2d) * world, "d2h_bytes_per_step": int(world * rows * 4),
+               "steps": e2e_steps,
+               "path": ("pinned host -> cudaMemcpyAsync -> d3s_sample -> ids to host" if world == 1 else
+                        "per rank: pinned host -> cudaMemcpyAsync -> d3s_sample writing into rank 0's "
+                        "result over NVLink (d3s_gather); rank 0: the N ids to host")}
         del hx
 
     cpu = None
     latency = None
+    configs = None
     if rank == 0 and world == 1:
         if not args.no_latency:
             latency = c1_latency(ctx, torch)
+        if not args.no_configs:
+            configs = {"c2": measure_c2(ctx, torch),
+                       "c3": {f"B{B}": measure_c3(ctx, torch, B, 20, 5) for B in (1, 64, 1024)},
+                       "c4": measure_c4(ctx, torch, 200)}
         if not args.no_cpu_baseline:
             n = min(rows, 16384)
             cpu = cpu_baseline(synth.to_host_logits(x[:n]), T[:n].cpu().numpy(), p[:n].cpu().numpy(),
@@ -378,7 +645,8 @@ def run_ours(args):
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows_per_gpu": rows, "V": V, "global_batch": world * rows,
-                       "parallelism": f"rows sharded over {world} GPU(s), ids gathered to rank 0",
+                       "parallelism": (f"rows sharded over {world} GPUs, ids written into rank 0's "
+                                       "result over NVLink" if world > 1 else "one GPU"),
                        "l2": "inputs 1.07 GB per GPU > 126 MB L2 (no flush needed)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
@@ -386,13 +654,19 @@ def run_ours(args):
                                    "sample_select_kernel + sample_wide_kernel (empty hand-off)",
                          "kernel_ms": kernel_ms, "kernel_ms_max_over_ranks": kernel_ms_max,
                          "bytes_per_launch": bytes_per_launch},
+            "per_rank_ms": [{"rank": r, "step_loop": v[0], "sample_mean": v[1], "collect_mean": v[2]}
+                            for r, v in enumerate(per_rank)],
             "clocks": clocks,
             "e2e": e2e,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": (3 + (2 if world > 1 else 0)) * args.steps,
             "cpu_baseline": cpu,
             "latency": latency,
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
+    if gather is not None:
+        barrier()
+        gather.close()
     ctx.close()
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -425,157 +699,39 @@ def load_tflops():
 
 
 def run_c3(args):
-    """Config 3: the lm_head projection (h [B, 2048] x W [4097, 2048]^T, bf16
-    logits) and the fused projection + sample call, one GPU."""
+    """Config 3 on its own line: the lm_head projection and the fused
+    projection + sample call at --batch B."""
     import torch
 
     import d3s
-    import synth
     torch.cuda.set_device(0)
-    B, D = args.batch, 2048
     ctx = d3s.Context(0)
-    ctx.reserve(max(B, 1024))
-    h, W = synth.c3_inputs(B, seed=7)
-    logits = torch.empty(B, V, dtype=torch.bfloat16, device="cuda")
-    ids = torch.empty(B, dtype=torch.int32, device="cuda")
-    seeds = torch.arange(B, dtype=torch.int64, device="cuda")
-    # the weight (16.8 MB) fits in L2: flush between projection launches so each one
-    # reads W from HBM, as a decode step that ran the backbone in between would. The
-    # flush READS 256 MB (a sum), leaving clean lines: a written buffer would leave
-    # dirty lines whose write-back competes with the projection's reads.
-    flush_buf = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
-    flush_out = torch.empty((), dtype=torch.float32, device="cuda")
-
-    class _Flush:
-        @staticmethod
-        def zero_():
-            torch.sum(flush_buf, dim=0, out=flush_out)
-
-    flush = _Flush()
-    st = torch.cuda.current_stream()
-
-    def proj():
-        ctx.lmhead(h, W, out=logits)
-
-    def fused():
-        ctx.lmhead_sample(h, W, logits, ids, temperature=0.7, top_p=0.7, top_k=30,
-                          noise=d3s.NOISE_SEEDS, seeds=seeds)
-
-    evs = []
-    for i in range(args.warmup + args.steps):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(st)
-        proj()
-        b.record(st)
-        if i >= args.warmup:
-            evs.append((a, b))
-    torch.cuda.synchronize()
-    proj_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    evs = []
-    for i in range(args.warmup + args.steps):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(st)
-        fused()
-        b.record(st)
-        if i >= args.warmup:
-            evs.append((a, b))
-    torch.cuda.synchronize()
-    ctx.check()
-    fused_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    peak_gbs, gkind = load_peaks()
-    peak_tf, tkind = load_tflops()
-    bytes_ = V * D * 2 + B * D * 2 + B * V * 2
-    flops = 2.0 * B * V * D
-    gbs = bytes_ / (proj_ms / 1e3) / 1e9
-    tfs = flops / (proj_ms / 1e3) / 1e12
-    tensor = B > 64
-    line = {
-        "metric": "lm_head + sample rows/s (config 3)", "value": B / (fused_ms / 1e3), "unit": "rows/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fused_ms,
-        "higher_is_better": True, "dtype": "bf16 x bf16 -> f32 accumulate -> bf16 logits",
-        "data": "synthetic", "config": {"workload": f"config3: h bf16 [{B}, {D}] ~N(0,1), W bf16 [{V}, {D}] "
-                                        "~N(0,0.02), T 0.7, top_p 0.7, top_k 30, per-row seeds",
-                                        "l2": "256 MB buffer read between launches"},
-        "projection_ms": proj_ms,
-        "projection_kernel": "lmhead_gemv_kernel" if B <= 8 else "lmhead_gemm_kernel (tcgen05)",
-        "roofline": ({"bound": "tensor", "achieved": tfs, "peak": peak_tf, "unit": "TFLOP/s",
-                      "frac": tfs / peak_tf, "peak_source": tkind} if tensor else
-                     {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s",
-                      "frac": gbs / peak_gbs, "peak_source": gkind}),
-        "hbm_gbs": gbs, "tflops": tfs,
-    }
+    r = measure_c3(ctx, torch, args.batch, args.steps, args.warmup)
+    line = {"metric": "lm_head + sample rows/s (config 3)", "value": r["fused_rows_per_s"],
+            "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["fused_us"] / 1e3, "higher_is_better": True,
+            "dtype": "bf16 x bf16 -> f32 accumulate -> bf16 logits", "data": "synthetic",
+            "config": {"workload": f"config3: h bf16 [{args.batch}, 2048] ~N(0,1), W bf16 [{V}, 2048] "
+                                   "~N(0,0.02), T 0.7, top_p 0.7, top_k 30, per-row seeds",
+                       "l2": "256 MB buffer read between launches"}, **r}
     print(json.dumps(line), flush=True)
     ctx.close()
 
 
 def run_c4(args):
-    """Config 4: 512 streams x 9 codebook heads per frame (bf16 [512, 1024] rows,
-    Zipf-biased), T 1.0, top_p 0.9, top_k 30, per-stream keys advanced in
-    tower_decode_step order; plus each frame's main + retry draw on a [512, 4097]
-    backbone row. One GPU, all frames' logits generated up front per frame set."""
+    """Config 4 on its own line."""
     import torch
 
     import d3s
-    import synth
     torch.cuda.set_device(0)
-    S, H, Vh = 512, 9, 1024
     ctx = d3s.Context(0)
-    ctx.reserve(2 * S)
-    bias = synth.zipf_bias(Vh, 11)
-    heads = [synth.c4_logits(S, seed=100 + j, V=Vh, bias=bias) for j in range(H)]
-    xb = synth.c1_rows(S, seed=5).to(torch.bfloat16)
-    states = torch.randint(0, 2**31 - 1, (S, 2), dtype=torch.int32, device="cuda")
-    hist = torch.zeros(S, 16, dtype=torch.int32, device="cuda")
-    hl = torch.zeros(S, dtype=torch.int32, device="cuda")
-    sub = torch.empty(S, 2 + H, 2, dtype=torch.int32, device="cuda")
-    ids = torch.empty(S, dtype=torch.int32, device="cuda")
-
-    def frame():
-        ctx.keys_next(states, 2 + H, sub=sub)
-        ctx.frame_main(xb, sub, hist, hl, temperature=1.0, top_p=0.9, top_k=30,
-                       semantic_start=1000, code_vocab=4096, eos_id=7)
-        for j in range(H):
-            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9, top_k=30)
-
-    def heads_only():
-        for j in range(H):
-            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9, top_k=30)
-
-    frames = max(1, args.frames)
-    frame_ms = _events_ms(torch, frame, frames)
-    heads_ms = _events_ms(torch, heads_only, frames)
-    ctx.check()
-    # the same frame captured once in a CUDA graph and replayed (no per-call host work)
-    gs = torch.cuda.Stream()
-    gs.wait_stream(torch.cuda.current_stream())
-    graph = torch.cuda.CUDAGraph()
-
-    def frame_on(stream):
-        ctx.keys_next(states, 2 + H, sub=sub, stream=stream)
-        ctx.frame_main(xb, sub, hist, hl, temperature=1.0, top_p=0.9, top_k=30,
-                       semantic_start=1000, code_vocab=4096, eos_id=7, stream=stream)
-        for j in range(H):
-            ctx.sample_rows_keys(heads[j], ids, sub[:, 2 + j], temperature=1.0, top_p=0.9,
-                                 top_k=30, stream=stream)
-
-    with torch.cuda.stream(gs):
-        with torch.cuda.graph(graph, stream=gs):
-            frame_on(gs)
-    torch.cuda.synchronize()
-    graph_ms = _events_ms(torch, graph.replay, frames)
-    ctx.check()
-    line = {
-        "metric": "tower head rows/s (config 4)", "value": S * H / (heads_ms / 1e3), "unit": "rows/s",
-        "n_gpus": 1, "frames": frames, "ms_per_frame_heads": heads_ms, "ms_per_frame_all": frame_ms,
-        "frame_rows_per_s": S * (H + 2) / (frame_ms / 1e3), "ms_per_frame_graph": graph_ms,
-        "frame_rows_per_s_graph": S * (H + 2) / (graph_ms / 1e3), "higher_is_better": True,
-        "dtype": "bf16 logits, f32 math", "data": "synthetic",
-        "config": {"workload": "config4: 512 streams x 9 heads, V=1024 bf16 ~N(0,2.5)+Zipf(1.1); "
-                               "frame main+retry on [512, 4097] bf16; T 1.0, top_p 0.9, top_k 30"},
-        "note": "a head launch is 512 rows: launch-bound; rows stay in L2",
-    }
+    r = measure_c4(ctx, torch, args.frames)
+    line = {"metric": "tower head rows/s (config 4)", "value": r["head_rows_per_s"], "unit": "rows/s",
+            "n_gpus": 1, "higher_is_better": True, "dtype": "bf16 logits, f32 math",
+            "data": "synthetic",
+            "config": {"workload": "config4: 512 streams x 9 heads, V=1024 bf16 ~N(0,2.5)+Zipf(1.1); "
+                                   "frame main+retry on [512, 4097] bf16; T 1.0, top_p 0.9, top_k 30"},
+            **r}
     print(json.dumps(line), flush=True)
     ctx.close()
 

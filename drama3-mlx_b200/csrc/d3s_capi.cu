@@ -16,18 +16,15 @@
 struct d3s_ctx {
   int device = 0;
   d3s::Scratch scratch;
-  // staging for the host-pointer entry point (d3_sample)
-  float *h_logits_dev = nullptr;
-  int32_t *ids_dev = nullptr;
-  int32_t *status_dev = nullptr;
-  size_t logits_cap = 0;  // floats
-  size_t rows_cap = 0;
+  // d3_sample's device staging: the logits, then at a 16-byte boundary the
+  // call's error word (+ 12 bytes of padding), its N ids and its N statuses
+  unsigned char *stage_dev = nullptr;
+  size_t stage_cap = 0;  // bytes
   cudaStream_t stream = nullptr;
   d3s::FrameScratch frame;  // d3s_frame_main's per-draw arrays
   float *lm_ws = nullptr;   // d3s_lmhead's split-K partials
   int64_t lm_ws_cap = 0;    // floats
-  void *pinned = nullptr;   // d3_sample's host staging: logits, ids + status, error word
-  size_t pinned_cap = 0;    // bytes
+  void *pinned = nullptr;   // d3_sample's host staging (stage_cap bytes), laid out as stage_dev
 };
 
 namespace {
@@ -319,8 +316,7 @@ void d3s_ctx_destroy(d3s_ctx *ctx) {
   cudaFree(ctx->scratch.counters);
   cudaFree(ctx->scratch.heads);
   cudaFree(ctx->scratch.cands);
-  cudaFree(ctx->h_logits_dev);
-  cudaFree(ctx->ids_dev);  // status_dev lives in the same allocation
+  cudaFree(ctx->stage_dev);
   cudaFreeHost(ctx->pinned);
   cudaFree(ctx->frame.keys);
   cudaFree(ctx->lm_ws);
@@ -594,52 +590,13 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
   if (rc != D3S_OK) return rc;
   std::lock_guard<std::mutex> lk(g_default_mu);
   DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(D3S_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
   cudaError_t e;
   if (!ctx->stream) {
     e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
   }
-  const size_t nl = (size_t)N * (size_t)V;
-  if (nl > ctx->logits_cap) {
-    cudaFree(ctx->h_logits_dev);
-    ctx->h_logits_dev = nullptr;
-    ctx->logits_cap = 0;
-    e = cudaMalloc(&ctx->h_logits_dev, nl * sizeof(float));
-    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "logits staging: %s", cudaGetErrorString(e));
-    ctx->logits_cap = nl;
-  }
-  if ((size_t)N > ctx->rows_cap) {
-    cudaFree(ctx->ids_dev);
-    ctx->ids_dev = nullptr;
-    ctx->status_dev = nullptr;
-    ctx->rows_cap = 0;
-    // ids then status in one allocation: one copy brings both back
-    e = cudaMalloc(&ctx->ids_dev, 2 * (size_t)N * sizeof(int32_t));
-    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "ids staging: %s", cudaGetErrorString(e));
-    ctx->status_dev = ctx->ids_dev + N;
-    ctx->rows_cap = (size_t)N;
-  }
-  // pinned host staging: the logits, then ids + status, then the error word
-  const size_t pin = nl * sizeof(float) + 2 * (size_t)ctx->rows_cap * sizeof(int32_t) + 16;
-  if (pin > ctx->pinned_cap) {
-    cudaFreeHost(ctx->pinned);
-    ctx->pinned = nullptr;
-    ctx->pinned_cap = 0;
-    e = cudaMallocHost(&ctx->pinned, pin);
-    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "host staging: %s", cudaGetErrorString(e));
-    ctx->pinned_cap = pin;
-  }
-  if (N == 0) return D3S_OK;
-  float *h_logits = static_cast<float *>(ctx->pinned);
-  int32_t *h_ids = reinterpret_cast<int32_t *>(h_logits + nl);
-  int32_t *h_err = h_ids + 2 * N;
-  d3s_seed(nullptr, seed);  // m_seed(seed), src/testapi.c:159
-  std::memcpy(h_logits, logits, nl * sizeof(float));
-  e = cudaMemcpyAsync(ctx->h_logits_dev, h_logits, nl * sizeof(float), cudaMemcpyHostToDevice,
-                      ctx->stream);
-  if (e != cudaSuccess) return cuda_fail(e, "logits upload");
   d3s_request r{};
-  r.logits = ctx->h_logits_dev;
   r.dtype = D3S_F32;
   r.N = N;
   r.V = V;
@@ -648,31 +605,64 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
   r.top_p = top_p;
   r.top_k = top_k;
   r.noise = D3S_NOISE_KEY;
-  r.ids = ctx->ids_dev;
-  r.status = ctx->status_dev;
+  r.logits = logits;  // placeholders for the argument check; replaced below
+  r.ids = out;
   rc = check_request(&r);
   if (rc != D3S_OK) return rc;
+  if (N == 0) return D3S_OK;
+  // One staging layout on both sides: [logits | error word, pad | ids | status].
+  // One copy uploads the logits with a zeroed error word, one brings the error
+  // word, the ids and the statuses back.
+  const size_t nl = (size_t)N * (size_t)V;
+  const size_t tail = (nl * sizeof(float) + 15) & ~(size_t)15;
+  const size_t need = tail + 16 + 2 * (size_t)N * sizeof(int32_t);
+  if (need > ctx->stage_cap) {
+    cudaStreamSynchronize(ctx->stream);  // the old buffers may be in use by queued work
+    cudaFree(ctx->stage_dev);
+    cudaFreeHost(ctx->pinned);
+    ctx->stage_dev = nullptr;
+    ctx->pinned = nullptr;
+    ctx->stage_cap = 0;
+    e = cudaMalloc(&ctx->stage_dev, need);
+    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "d3_sample staging: %s", cudaGetErrorString(e));
+    e = cudaMallocHost(&ctx->pinned, need);
+    if (e != cudaSuccess) {
+      cudaFree(ctx->stage_dev);
+      ctx->stage_dev = nullptr;
+      return fail(D3S_ERR_NOMEM, "host staging: %s", cudaGetErrorString(e));
+    }
+    ctx->stage_cap = need;
+  }
+  rc = reserve_scratch(ctx, N);
+  if (rc != D3S_OK) return rc;
+  unsigned char *hp = static_cast<unsigned char *>(ctx->pinned);
+  std::memcpy(hp, logits, nl * sizeof(float));
+  std::memset(hp + nl * sizeof(float), 0, tail + 16 - nl * sizeof(float));
+  e = cudaMemcpyAsync(ctx->stage_dev, hp, tail + 16, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "logits upload");
+  int32_t *ids_dev = reinterpret_cast<int32_t *>(ctx->stage_dev + tail + 16);
+  r.logits = ctx->stage_dev;
+  r.ids = ids_dev;
+  r.status = ids_dev + N;
+  d3s_seed(nullptr, seed);  // m_seed(seed), src/testapi.c:159
   d3s_key sub;
   take_subkey(nullptr, &sub);
   r.key = sub;
-  rc = d3s_sample(ctx, &r, ctx->stream);
-  if (rc != D3S_OK) return rc;
-  // ids and status (adjacent on the device), then the context's error word
-  e = cudaMemcpyAsync(h_ids, ctx->ids_dev, 2 * (size_t)N * sizeof(int32_t), cudaMemcpyDeviceToHost,
-                      ctx->stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(h_err, ctx->scratch.counters + 2, sizeof(int32_t), cudaMemcpyDeviceToHost,
-                        ctx->stream);
+  d3s::KArgs a = to_kargs(&r, ctx);
+  a.error = reinterpret_cast<int32_t *>(ctx->stage_dev + tail);  // this call's own error word
+  rc = d3s::launch_sample(a, ctx->scratch, ctx->stream);
+  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "sampler launch");
+  e = cudaMemcpyAsync(hp + tail, ctx->stage_dev + tail, 16 + 2 * (size_t)N * sizeof(int32_t),
+                      cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return cuda_fail(e, "d3_sample");
+  const int32_t *h_err = reinterpret_cast<const int32_t *>(hp + tail);
+  const int32_t *h_ids = h_err + 4;
   std::memcpy(out, h_ids, (size_t)N * sizeof(int32_t));
   int bad = 0;
   for (int i = 0; i < N; i++) bad += h_ids[N + i] != D3S_ROW_OK;
-  if (*h_err) {
-    cudaMemsetAsync(ctx->scratch.counters + 2, 0, sizeof(uint32_t), ctx->stream);
-    cudaStreamSynchronize(ctx->stream);
+  if (*h_err)
     return fail(D3S_ERR_CUDA, "a sampler kernel gave up waiting for a row copy (rows left unsampled)");
-  }
   if (bad) return fail(D3S_ERR_NONFINITE, "%d row(s) had non-finite logits", bad);
   return D3S_OK;
 }

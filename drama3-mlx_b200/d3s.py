@@ -41,10 +41,14 @@ EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split"
            "d3s_sample_noise", "d3s_sample_with_noise", "d3s_sample_top_k_top_p", "d3s_sample",
            "d3s_debug_math", "d3s_debug_div_check", "d3s_ctx_check", "d3s_sample_rows_static",
            "d3_sample", "d3s_last_status", "d3s_keys_next", "d3s_frame_main", "d3s_lmhead",
-           "d3s_lmhead_sample", "d3s_codes_write_npy")
+           "d3s_lmhead_sample", "d3s_codes_write_npy", "d3s_static_check",
+           "d3s_static_debug_set_error", "d3s_gather_create", "d3s_gather_export",
+           "d3s_gather_attach", "d3s_gather_begin", "d3s_gather_end", "d3s_gather_release",
+           "d3s_gather_check", "d3s_gather_destroy", "d3s_gather_copy_result")
 RAS_WINDOW = 16
 FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
 STATIC_MAX_ROWS = 4096
+GATHER_HANDLE_BYTES = 64
 
 
 class D3SError(RuntimeError):
@@ -128,6 +132,18 @@ def lib() -> ctypes.CDLL:
         L.d3s_debug_div_check.argtypes = [vp, vp, i32, u64, u64, u64, vp, vp, vp]
         L.d3s_ctx_check.argtypes = [vp]
         L.d3s_sample_rows_static.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp]
+        L.d3s_static_check.argtypes = [vp]
+        L.d3s_gather_create.argtypes = [i32, i32, i32, i64, ctypes.POINTER(vp)]
+        L.d3s_gather_export.argtypes = [vp, vp]
+        L.d3s_gather_attach.argtypes = [vp, vp]
+        L.d3s_gather_begin.argtypes = [vp, i64, ctypes.POINTER(vp), vp]
+        L.d3s_gather_end.argtypes = [vp, i64, ctypes.POINTER(vp), vp]
+        L.d3s_gather_release.argtypes = [vp, i64, vp]
+        L.d3s_gather_check.argtypes = [vp, vp]
+        L.d3s_gather_copy_result.argtypes = [vp, i64, vp, vp]
+        L.d3s_gather_destroy.argtypes = [vp]
+        L.d3s_gather_destroy.restype = None
+        L.d3s_static_debug_set_error.argtypes = [ctypes.c_int32, vp]
         L.d3_sample.argtypes = [ctypes.POINTER(ctypes.c_float), i32, i32, f32, i32, f32,
                                 ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_int32)]
         L.d3_sample.restype = None
@@ -181,11 +197,40 @@ def codes_write_npy(path, frames, n_codebooks: int) -> None:
 
 
 def sample_rows_static(logits, ids, temperature, top_p, top_k, seeds, stream=None) -> None:
-    """d3s_sample_rows_static on CUDA tensors (all per-row arrays required)."""
+    """d3s_sample_rows_static on CUDA tensors: logits [N, V] (float32 or
+    bfloat16, unit stride along V), and the per-row arrays, all required and
+    contiguous on the logits' device: temperature and top_p float32 [N], top_k
+    int32 [N], seeds int64 or uint64 [N], ids int32 [N] (written)."""
+    import torch
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a [N, V] tensor with unit stride along V")
     N, V = logits.shape
+    want = [("temperature", temperature, (torch.float32,)), ("top_p", top_p, (torch.float32,)),
+            ("top_k", top_k, (torch.int32,)), ("seeds", seeds, (torch.int64, torch.uint64)),
+            ("ids", ids, (torch.int32,))]
+    for name, t, dtypes in want:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a tensor")
+        if t.dtype not in dtypes:
+            raise TypeError(f"{name} must be {' or '.join(map(str, dtypes))}, got {t.dtype}")
+        if t.numel() != N or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous tensor of {N} elements")
+        if t.device != logits.device:
+            raise ValueError(f"{name} is on {t.device}, the logits on {logits.device}")
     _check(lib().d3s_sample_rows_static(_ptr(logits), _dtype_code(logits), N, V, logits.stride(0),
                                         _ptr(temperature), _ptr(top_p), _ptr(top_k), _ptr(seeds),
                                         _ptr(ids), _stream_ptr(stream)))
+
+
+def static_check(stream=None) -> None:
+    """d3s_static_check: waits for `stream`, raises D3SError if a
+    d3s_sample_rows_static call since the last check recorded a failure."""
+    _check(lib().d3s_static_check(_stream_ptr(stream)))
+
+
+def static_debug_set_error(value: int, stream=None) -> None:
+    """Test hook: set the static scratch's error word (no failure is caused)."""
+    _check(lib().d3s_static_debug_set_error(value, _stream_ptr(stream)))
 
 
 # ---- the reference's test entry point ----
@@ -211,7 +256,9 @@ def last_status() -> int:
 # ---- device API on torch tensors ----
 
 def _ptr(t) -> int | None:
-    return None if t is None else t.data_ptr()
+    if t is None or isinstance(t, int):
+        return t
+    return t.data_ptr()
 
 
 def _stream_ptr(stream) -> int | None:
@@ -324,7 +371,9 @@ class Context:
 
     def sample_rows(self, logits, ids, *, temperature, top_p, top_k, seeds, status=None,
                     kept=None, stream=None) -> None:
-        """Per-row parameters (tensors or scalars) and per-row seeds (int64 tensor)."""
+        """Per-row parameters (tensors or scalars) and per-row seeds (int64 tensor).
+        ids: an int32 tensor of N, or a raw device address of N int32 (the
+        slot a Gather gives, which may be another GPU's memory)."""
         import torch
 
         def split(x):
@@ -431,3 +480,67 @@ class Context:
                                          _ptr(ex), _stream_ptr(stream)))
         torch.cuda.synchronize()
         return int(bad.item()), ex.cpu().tolist()
+
+
+class Gather:
+    """d3s_gather: the ids of rows sharded over the ranks of one node written
+    straight into rank 0's result by each rank's sampler (NVLink peer stores),
+    with a completion counter in rank 0's memory. `exchange(handle or None)`
+    is the caller's channel for rank 0's 64-byte IPC handle: it is called once
+    on every rank with rank 0's handle (bytes) on rank 0 and None elsewhere,
+    and returns rank 0's handle on every rank."""
+
+    def __init__(self, device: int, world: int, rank: int, rows: int, exchange):
+        self.rank, self.world, self.rows = rank, world, rows
+        self._h = ctypes.c_void_p()
+        _check(lib().d3s_gather_create(device, world, rank, rows, ctypes.byref(self._h)))
+        try:
+            mine = None
+            if rank == 0:
+                buf = ctypes.create_string_buffer(GATHER_HANDLE_BYTES)
+                _check(lib().d3s_gather_export(self._h, buf))
+                mine = buf.raw
+            handle = exchange(mine)
+            if rank != 0:
+                buf = ctypes.create_string_buffer(bytes(handle), GATHER_HANDLE_BYTES)
+                _check(lib().d3s_gather_attach(self._h, buf))
+        except Exception:
+            self.close()
+            raise
+
+    def begin(self, step: int, stream=None) -> int:
+        """Device address where this rank's sampler writes the ids of its rows at `step`."""
+        p = ctypes.c_void_p()
+        _check(lib().d3s_gather_begin(self._h, step, ctypes.byref(p), _stream_ptr(stream)))
+        return int(p.value)
+
+    def end(self, step: int, stream=None) -> int | None:
+        """After the sampler: signal (ranks > 0) or wait for every rank (rank 0).
+        Rank 0 gets the device address of the step's N ids."""
+        p = ctypes.c_void_p()
+        _check(lib().d3s_gather_end(self._h, step, ctypes.byref(p), _stream_ptr(stream)))
+        return int(p.value) if p.value else None
+
+    def release(self, step: int, stream=None) -> None:
+        _check(lib().d3s_gather_release(self._h, step, _stream_ptr(stream)))
+
+    def copy_result(self, step: int, out, stream=None):
+        """Rank 0: the N ids of `step` into `out` (int32 CUDA tensor of N), on the stream."""
+        if out.dtype.itemsize != 4 or out.numel() != self.rows or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous int32 tensor of {self.rows} ids")
+        _check(lib().d3s_gather_copy_result(self._h, step, _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def check(self, stream=None) -> None:
+        _check(lib().d3s_gather_check(self._h, _stream_ptr(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            lib().d3s_gather_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -4,8 +4,14 @@ Rows are independent, so a batch of N rows is split into contiguous ranges,
 rank r taking rows [r*N/G, (r+1)*N/G); each rank samples its own rows with its
 own per-row seeds (a row's seed is its global row index's seed, so the result
 does not depend on G), and the int32 ids are gathered to one rank. There is no
-other exchange. The functions take any torch.distributed process group: NCCL
-with CUDA tensors on the GPUs, gloo with CPU tensors in the tests.
+other exchange.
+
+On the GPUs the gather is d3s.Gather (the library's d3s_gather): each rank's
+sampler writes its ids straight into rank 0's result over NVLink, so no
+collective runs per step; `handle_exchange` is the one-time channel that hands
+rank 0's IPC handle to the other ranks. `gather_ids` is the same gather as one
+torch.distributed collective (any process group: gloo with CPU tensors in the
+tests).
 """
 
 from __future__ import annotations
@@ -16,6 +22,22 @@ def shard_range(n_rows: int, world: int, rank: int) -> tuple[int, int]:
     if world < 1 or not 0 <= rank < world or n_rows < 0:
         raise ValueError(f"bad shard: n_rows={n_rows} world={world} rank={rank}")
     return n_rows * rank // world, n_rows * (rank + 1) // world
+
+
+def handle_exchange(group=None, src: int = 0):
+    """The exchange function d3s.Gather takes: rank `src` passes its handle
+    (bytes), the others None, and every rank gets the source's handle back
+    (one broadcast of a Python object over the process group)."""
+    import torch.distributed as dist
+
+    def exchange(mine):
+        obj = [mine]
+        dist.broadcast_object_list(obj, src=src, group=group)
+        if not isinstance(obj[0], (bytes, bytearray)):
+            raise RuntimeError("rank 0 sent no gather handle")
+        return bytes(obj[0])
+
+    return exchange
 
 
 def gather_ids(ids, n_rows: int, world: int, rank: int, dst: int = 0, group=None):

@@ -176,8 +176,8 @@ D3S_API int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64
 
 /* No counterpart in the reference. For callers that cannot allocate device
  * memory while they sample: a serving engine that budgets every device byte
- * up front, a real-time audio thread that cannot wait on cudaMalloc's implicit
- * device synchronisation, code running inside someone else's stream capture.
+ * up front and forbids allocation once it serves, or a real-time audio thread
+ * that cannot wait on cudaMalloc's implicit device synchronisation.
  * Same results as d3s_sample with D3S_NOISE_SEEDS and per-row temperature,
  * top_p and top_k (all device arrays of N, as are the logits and ids); no
  * context is needed. Its scratch is one fixed array in the library shared by
@@ -185,11 +185,61 @@ D3S_API int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64
  * and two calls whose kernels overlap on the GPU (different streams without an
  * ordering between them) race on it. The first call on each device looks up
  * the array's device address (cudaGetSymbolAddress); make that first call
- * before capturing a CUDA graph. Nothing is allocated, on any call. */
+ * before any stream capture. Nothing is allocated, on any call.
+ * A kernel that gives up a bounded wait (a row copy that never completed)
+ * records it in the array's error word and leaves rows' ids unwritten; the
+ * word stays set across calls until d3s_static_check reads it. */
 D3S_API int d3s_sample_rows_static(const void *logits_dev, int dtype, int N, int V, int64_t ld,
                                    const float *temperature_dev, const float *top_p_dev,
                                    const int32_t *top_k_dev, const uint64_t *seeds_dev,
                                    int32_t *ids_dev, void *stream);
+
+/* No counterpart in the reference. Waits for the work queued on `stream`,
+ * then reads and clears the error word of d3s_sample_rows_static's scratch on
+ * the current device: D3S_OK when no call since the last check gave up a
+ * wait, else D3S_ERR_CUDA (the ids of the calls since the last check are
+ * undefined). Allocates nothing. */
+D3S_API int d3s_static_check(void *stream);
+
+/* Test hook (no counterpart in the reference): stores `value` in the error
+ * word that d3s_static_check reads, on the current device, ordered on
+ * `stream`, so a test can see a recorded failure reported without stalling a
+ * copy. */
+D3S_API int d3s_static_debug_set_error(int32_t value, void *stream);
+
+/* ---- rows sharded over the GPUs of a node: the gather of ids to rank 0 ---- */
+
+/* No single counterpart in the reference (it samples on one device); this is
+ * the id gather that sharding the rows over G GPUs needs, one process per GPU.
+ * Rank r samples rows [r N / G, (r + 1) N / G) of an N-row batch and its
+ * sampler writes their ids straight into rank 0's result (a CUDA IPC mapping
+ * of rank 0's buffer, plain stores over NVLink), so no collective runs after
+ * the sampler; a counter in rank 0's memory, raised by each rank after its
+ * sampler (release at system scope) and waited on by rank 0 (acquire, with a
+ * 5 s limit that sets the gather's error word instead of hanging), marks the
+ * step complete. The result has two slots (step parity): a rank writes step s
+ * only after rank 0 released step s - 2.
+ * Use: every rank d3s_gather_create; rank 0 d3s_gather_export, the 64-byte
+ * handle passed to the other ranks by the caller's own channel, which call
+ * d3s_gather_attach. Then per step s = 0, 1, 2, ... on every rank:
+ * d3s_gather_begin (the ids pointer for this rank's rows), the sampler with
+ * req.ids = that pointer, d3s_gather_end; rank 0 reads the N ids of step s at
+ * the result pointer d3s_gather_end gave, after it on its stream, then calls
+ * d3s_gather_release. */
+#define D3S_GATHER_HANDLE_BYTES 64
+typedef struct d3s_gather d3s_gather;
+D3S_API int d3s_gather_create(int device, int world, int rank, int64_t rows, d3s_gather **out);
+D3S_API int d3s_gather_export(d3s_gather *g, void *handle);
+D3S_API int d3s_gather_attach(d3s_gather *g, const void *handle);
+D3S_API int d3s_gather_begin(d3s_gather *g, int64_t step, int32_t **ids_dev, void *stream);
+D3S_API int d3s_gather_end(d3s_gather *g, int64_t step, int32_t **result_dev, void *stream);
+D3S_API int d3s_gather_release(d3s_gather *g, int64_t step, void *stream);
+/* Rank 0: copy the N ids of `step` (after d3s_gather_end) to dst_dev, on `stream`. */
+D3S_API int d3s_gather_copy_result(d3s_gather *g, int64_t step, int32_t *dst_dev, void *stream);
+/* Waits for `stream`; D3S_ERR_CUDA (and clears it) when a wait of this rank
+ * gave up since the last check. */
+D3S_API int d3s_gather_check(d3s_gather *g, void *stream);
+D3S_API void d3s_gather_destroy(d3s_gather *g);
 
 /* ---- one decode frame: tower_decode_step's draws (src/tower.c:405-452) ---- */
 

@@ -76,3 +76,32 @@ def test_shard_range_covers_rows_once():
                 assert b == c and b - a >= d - c - 1 and d - c >= b - a - 1
     with pytest.raises(ValueError):
         shard.shard_range(10, 2, 2)
+
+
+def _exchange_main(rank, world, port, out_path):
+    for p in (ROOT / "drama3-mlx_b200",):
+        sys.path.insert(0, str(p))
+    import torch.distributed as dist
+
+    import shard
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        handle = bytes(range(64)) if rank == 0 else None
+        got = shard.handle_exchange()(handle)
+        Path(f"{out_path}.{rank}").write_bytes(got)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_handle_reaches_every_rank(tmp_path, world):
+    """The one-time exchange of rank 0's 64-byte IPC handle that the NVLink id
+    gather needs: every rank receives rank 0's bytes unchanged."""
+    import torch.multiprocessing as mp
+    out = tmp_path / "handle"
+    mp.spawn(_exchange_main, args=(world, free_port(), str(out)), nprocs=world, join=True)
+    for r in range(world):
+        assert Path(f"{out}.{r}").read_bytes() == bytes(range(64))

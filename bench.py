@@ -494,28 +494,65 @@ def run_ours(args):
     ids = torch.empty(rows, dtype=torch.int32, device="cuda")
     st = torch.cuda.current_stream()
     # N > 1: each rank's sampler writes its ids straight into rank 0's result
-    # over NVLink (d3s_gather); the step is complete on rank 0 once every
-    # rank's completion count has landed
-    gather = d3s.Gather(local, world, rank, world * rows, shard.handle_exchange()) \
+    # over NVLink (d3s_gather). A rank > 0 signals each step on a side stream
+    # (after an event of its sampler's stream), overlapping its next step; rank
+    # 0 completes the gather of step s on its own stream right after sampling
+    # step s + 1, when every rank's signal for s has landed, so its wait ends at
+    # once and never spins beside a sampler. Four slots let a rank run up to
+    # three steps ahead of rank 0's gather.
+    gather = d3s.Gather(local, world, rank, world * rows, shard.handle_exchange(), slots=4) \
         if world > 1 else None
     gather_out = torch.empty(world * rows, dtype=torch.int32, device="cuda") \
         if gather is not None and rank == 0 else None
-    step_no = [0]
+    side = torch.cuda.Stream() if gather is not None and rank != 0 else None
+    next_step = [0]     # the step the next sampler call writes
+    pending = []        # rank 0: sampled steps whose gather is not yet complete
 
     def target():
         """Where this step's ids go: the local tensor, or (N > 1) this rank's
-        rows of rank 0's result (waits until rank 0 released step - 2)."""
-        return gather.begin(step_no[0]) if gather is not None else ids
+        rows of rank 0's result (waits until rank 0 released step - slots)."""
+        return gather.begin(next_step[0], stream=st) if gather is not None else ids
 
     def sample(out):
         ctx.sample_rows(x, out, temperature=T, top_p=p, top_k=k, seeds=seeds)
 
-    def collect():
+    def finish(s_, host_out=None):
+        """Rank 0: wait for every rank's ids of step s_ (on the sampler's
+        stream), copy them to host_out if given, release the slot."""
+        gather.end(s_, stream=st)
+        if host_out is not None:
+            gather.copy_result(s_, gather_out, stream=st)
+            host_out.copy_(gather_out, non_blocking=True)
+        gather.release(s_, stream=st)
+
+    def collect(host_out=None, last=False):
+        """After a sampler call (N > 1). Ranks > 0: signal on the side stream.
+        Rank 0: complete the gather of the previous step (or, with last, of
+        every step still pending)."""
         if gather is None:
             return
-        gather.end(step_no[0])
-        gather.release(step_no[0])
-        step_no[0] += 1
+        s_ = next_step[0]
+        next_step[0] += 1
+        if rank != 0:
+            ev = torch.cuda.Event()
+            ev.record(st)
+            side.wait_event(ev)
+            gather.end(s_, stream=side)
+            return
+        pending.append(s_)
+        while len(pending) > (0 if last else 1):
+            finish(pending.pop(0), host_out)
+
+    def drain(host_out=None):
+        """End of a loop: rank 0 completes every pending step's gather; ranks
+        > 0 order their stream after their last signal."""
+        if gather is None:
+            return
+        if rank == 0:
+            while pending:
+                finish(pending.pop(0), host_out)
+        else:
+            st.wait_stream(side)
 
     def barrier():
         if world > 1:
@@ -534,6 +571,7 @@ def run_ours(args):
     for _ in range(args.warmup):
         sample(target())
         collect()
+    drain()
     barrier()
     uuid = str(getattr(torch.cuda.get_device_properties(local), "uuid", "") or "")
     phys = int((os.environ.get("CUDA_VISIBLE_DEVICES", "") or str(local)).split(",")[local]) \
@@ -549,6 +587,7 @@ def run_ours(args):
             kev[i][1].record(st)
             collect()
             kev[i][2].record(st)
+        drain()  # the job ends when rank 0 holds the last step's ids
         end.record(st)
         barrier()
     elapsed_local = start.elapsed_time(end)
@@ -588,23 +627,20 @@ def run_ours(args):
                 ctx.sample_rows(dx, did, temperature=dT, top_p=dp, top_k=dk, seeds=ds)
                 hids.copy_(did, non_blocking=True)
                 return
-            s_ = step_no[0]
-            ctx.sample_rows(dx, gather.begin(s_), temperature=dT, top_p=dp, top_k=dk, seeds=ds)
-            gather.end(s_)
-            if rank == 0:
-                gather.copy_result(s_, gather_out)
-                hids.copy_(gather_out, non_blocking=True)
-            gather.release(s_)
-            step_no[0] += 1
+            out = target()
+            ctx.sample_rows(dx, out, temperature=dT, top_p=dp, top_k=dk, seeds=ds)
+            collect(host_out=hids if rank == 0 else None)
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):
             e2e_step()
+        drain(hids if rank == 0 else None)
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(st)
         for _ in range(e2e_steps):
             e2e_step()
+        drain(hids if rank == 0 else None)
         b.record(st)
         barrier()
         e2e_ms = max(r[0] for r in over_ranks([a.elapsed_time(b)]))
@@ -654,8 +690,8 @@ def run_ours(args):
                                    "sample_select_kernel + sample_wide_kernel (empty hand-off)",
                          "kernel_ms": kernel_ms, "kernel_ms_max_over_ranks": kernel_ms_max,
                          "bytes_per_launch": bytes_per_launch},
-            "per_rank_ms": [{"rank": r, "step_loop": v[0], "sample_mean": v[1], "collect_mean": v[2]}
-                            for r, v in enumerate(per_rank)],
+            "per_rank_ms": [{"rank": r, "step_loop": v[0], "sample_mean": v[1],
+                             "gather_step_mean": v[2]} for r, v in enumerate(per_rank)],
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": (3 + (2 if world > 1 else 0)) * args.steps,

@@ -8,13 +8,16 @@
 // own kernels. Completion is a counter in rank 0's memory: each rank adds 1
 // (a release at system scope) after its sampler, and rank 0 waits (an acquire
 // spin with a time limit) until every rank's addition for the step has
-// landed. The result has two slots (step parity): a rank may write step s
-// only after rank 0 released step s - 2, so rank 0 can still read step s - 1
-// while the ranks write step s.
+// landed. The result has `slots` slots (step s in slot s mod slots): a rank
+// may write step s only after rank 0 released step s - slots, so rank 0 can
+// still read the last slots - 1 steps while the ranks write step s, and the
+// ranks may run up to slots - 1 steps ahead of rank 0's gather. Issued on a
+// side stream (after an event of the sampler's stream), the signal and the
+// wait overlap the next step's sampling.
 //
 // Layout of the allocation rank 0 owns (exported by cudaIpcGetMemHandle):
 //   [0, 256)                      control words: arrived, released
-//   [256, 256 + 8 N)              two slots of N int32 ids
+//   [256, 256 + 4 N slots)        `slots` slots of N int32 ids
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -26,6 +29,7 @@ struct d3s_gather {
   int device = 0;
   int world = 1, rank = 0;
   int64_t rows = 0;            // N, the ids of every rank together
+  int slots = 2;
   int64_t start = 0, stop = 0;  // this rank's rows
   unsigned char *base = nullptr;  // rank 0: its allocation; others: the IPC mapping
   bool opened = false;            // base is an IPC mapping (ranks > 0)
@@ -70,11 +74,11 @@ __global__ void gather_wait_kernel(const unsigned *word, unsigned target, int32_
   }
 }
 
-// *word = value with release semantics at system scope, after every earlier
-// access of this stream (the reads of a released slot).
+// *word = value with release semantics at system scope. The reads of the
+// released slot are earlier work of this stream, complete before this kernel
+// starts; the peers only write the slot after they observe the new value.
 __global__ void gather_publish_kernel(unsigned *word, unsigned value) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  __threadfence_system();
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(word), "r"(value) : "memory");
 }
 
@@ -109,18 +113,20 @@ struct DevScope {
 
 Ctrl *ctrl(const d3s_gather *g) { return reinterpret_cast<Ctrl *>(g->base); }
 int32_t *slot(const d3s_gather *g, int64_t step) {
-  return reinterpret_cast<int32_t *>(g->base + kCtrlBytes) + (step & 1) * g->rows;
+  return reinterpret_cast<int32_t *>(g->base + kCtrlBytes) + (step % g->slots) * g->rows;
 }
 
 }  // namespace
 
 extern "C" {
 
-int d3s_gather_create(int device, int world, int rank, int64_t rows, d3s_gather **out) {
+int d3s_gather_create(int device, int world, int rank, int64_t rows, int slots,
+                      d3s_gather **out) {
   if (!out) return gfail(D3S_ERR_ARG, "d3s_gather_create: null out");
   *out = nullptr;
-  if (world < 1 || rank < 0 || rank >= world || rows < 0 || rows > (int64_t)1 << 40)
-    return gfail(D3S_ERR_ARG, "d3s_gather_create: bad world / rank / rows");
+  if (world < 1 || rank < 0 || rank >= world || rows < 0 || rows > (int64_t)1 << 36 || slots < 2 ||
+      slots > 64)
+    return gfail(D3S_ERR_ARG, "d3s_gather_create: bad world / rank / rows / slots");
   DevScope d(device);
   if (!d.ok) return gfail(D3S_ERR_CUDA, "d3s_gather_create: cudaSetDevice failed");
   d3s_gather *g = new (std::nothrow) d3s_gather();
@@ -129,13 +135,15 @@ int d3s_gather_create(int device, int world, int rank, int64_t rows, d3s_gather 
   g->world = world;
   g->rank = rank;
   g->rows = rows;
+  g->slots = slots;
   g->start = rows * rank / world;
   g->stop = rows * (rank + 1) / world;
   cudaError_t e = cudaMalloc(&g->error_local, sizeof(int32_t));
   if (e == cudaSuccess) e = cudaMemset(g->error_local, 0, sizeof(int32_t));
   if (e == cudaSuccess && rank == 0) {
-    e = cudaMalloc(&g->base, kCtrlBytes + 2 * (size_t)rows * sizeof(int32_t));
-    if (e == cudaSuccess) e = cudaMemset(g->base, 0, kCtrlBytes + 2 * (size_t)rows * sizeof(int32_t));
+    const size_t bytes = kCtrlBytes + (size_t)slots * (size_t)rows * sizeof(int32_t);
+    e = cudaMalloc(&g->base, bytes);
+    if (e == cudaSuccess) e = cudaMemset(g->base, 0, bytes);
   }
   if (e != cudaSuccess) {
     cudaFree(g->error_local);
@@ -177,10 +185,11 @@ int d3s_gather_begin(d3s_gather *g, int64_t step, int32_t **ids_dev, void *strea
   if (!g || !ids_dev || step < 0) return gfail(D3S_ERR_ARG, "d3s_gather_begin: bad argument");
   if (!g->base) return gfail(D3S_ERR_ARG, "d3s_gather_begin: not attached");
   DevScope d(g->device);
-  // the slot of `step` is free once rank 0 released step - 2
-  if (step >= 2) {
+  // the slot of `step` is free once rank 0 released step - slots (rank 0
+  // releases in the order of its own stream, so it never waits here)
+  if (step >= g->slots && g->rank != 0) {
     gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        &ctrl(g)->released, (unsigned)(step - 1), g->error_local);
+        &ctrl(g)->released, (unsigned)(step - g->slots + 1), g->error_local);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return gcuda(e, "gather slot wait launch");
   }

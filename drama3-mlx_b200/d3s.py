@@ -133,7 +133,7 @@ def lib() -> ctypes.CDLL:
         L.d3s_ctx_check.argtypes = [vp]
         L.d3s_sample_rows_static.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp]
         L.d3s_static_check.argtypes = [vp]
-        L.d3s_gather_create.argtypes = [i32, i32, i32, i64, ctypes.POINTER(vp)]
+        L.d3s_gather_create.argtypes = [i32, i32, i32, i64, i32, ctypes.POINTER(vp)]
         L.d3s_gather_export.argtypes = [vp, vp]
         L.d3s_gather_attach.argtypes = [vp, vp]
         L.d3s_gather_begin.argtypes = [vp, i64, ctypes.POINTER(vp), vp]
@@ -490,10 +490,10 @@ class Gather:
     on every rank with rank 0's handle (bytes) on rank 0 and None elsewhere,
     and returns rank 0's handle on every rank."""
 
-    def __init__(self, device: int, world: int, rank: int, rows: int, exchange):
-        self.rank, self.world, self.rows = rank, world, rows
+    def __init__(self, device: int, world: int, rank: int, rows: int, exchange, slots: int = 2):
+        self.rank, self.world, self.rows, self.slots = rank, world, rows, slots
         self._h = ctypes.c_void_p()
-        _check(lib().d3s_gather_create(device, world, rank, rows, ctypes.byref(self._h)))
+        _check(lib().d3s_gather_create(device, world, rank, rows, slots, ctypes.byref(self._h)))
         try:
             mine = None
             if rank == 0:

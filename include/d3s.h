@@ -217,18 +217,26 @@ D3S_API int d3s_static_debug_set_error(int32_t value, void *stream);
  * the sampler; a counter in rank 0's memory, raised by each rank after its
  * sampler (release at system scope) and waited on by rank 0 (acquire, with a
  * 5 s limit that sets the gather's error word instead of hanging), marks the
- * step complete. The result has two slots (step parity): a rank writes step s
- * only after rank 0 released step s - 2.
+ * step complete. The result has `slots` (>= 2) slots, step s in slot
+ * s mod slots: a rank writes step s only after rank 0 released step
+ * s - slots, so the ranks may run up to slots - 1 steps ahead of rank 0's
+ * gather.
  * Use: every rank d3s_gather_create; rank 0 d3s_gather_export, the 64-byte
  * handle passed to the other ranks by the caller's own channel, which call
  * d3s_gather_attach. Then per step s = 0, 1, 2, ... on every rank:
- * d3s_gather_begin (the ids pointer for this rank's rows), the sampler with
- * req.ids = that pointer, d3s_gather_end; rank 0 reads the N ids of step s at
- * the result pointer d3s_gather_end gave, after it on its stream, then calls
- * d3s_gather_release. */
+ * d3s_gather_begin on the sampler's stream (it waits there until the slot is
+ * free and gives the ids pointer for this rank's rows), the sampler with
+ * req.ids = that pointer, then d3s_gather_end on a stream ordered after the
+ * sampler (the same one, or a side stream that waited for an event of it, so
+ * the signal / wait overlaps the next step's sampling); rank 0 reads the N ids
+ * of step s at the result pointer d3s_gather_end gave, after it on that
+ * stream, then calls d3s_gather_release there. Rank 0's own sampler does not
+ * wait for a free slot: its release of step s - slots must come before its
+ * sampler of step s in stream order. */
 #define D3S_GATHER_HANDLE_BYTES 64
 typedef struct d3s_gather d3s_gather;
-D3S_API int d3s_gather_create(int device, int world, int rank, int64_t rows, d3s_gather **out);
+D3S_API int d3s_gather_create(int device, int world, int rank, int64_t rows, int slots,
+                              d3s_gather **out);
 D3S_API int d3s_gather_export(d3s_gather *g, void *handle);
 D3S_API int d3s_gather_attach(d3s_gather *g, const void *handle);
 D3S_API int d3s_gather_begin(d3s_gather *g, int64_t step, int32_t **ids_dev, void *stream);

@@ -22,6 +22,7 @@
 // from global memory (L2) in each pass, selection by exact bisection on the
 // 64-bit (value, id) key, bitonic sort of the k winners in shared memory.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <map>
 #include <mutex>
@@ -1143,7 +1144,9 @@ __device__ __forceinline__ bool select_row(const KArgs &a, int row, int C,
                                            const unsigned long long *cs, const RowCands &Cs,
                                            uint2 key, const RowP &rp, float lse_lo, float lse_hi,
                                            unsigned long long *sk, float *scr, int lane) {
-  if (C > kCandCap) {  // more candidates than the list holds (ties): the wide kernel's exact path
+  // more candidates than the list holds (ties), or fewer than k (the top k
+  // reaches below every candidate: -inf entries): the wide kernel's exact path
+  if (C > kCandCap || C < rp.k) {
     if (lane == 0) defer_row(a, row);
     return true;
   }
@@ -1519,7 +1522,7 @@ __global__ void __launch_bounds__(32, RwBounds<NC>::kMinBlocks)
           if (lane >= d) incl += o;
         }
         C = __shfl_sync(kFull, incl, 31);
-        if (C > kCandCap) {
+        if (C > kCandCap || C < rp.k) {  // C < k: the top k reaches below every candidate (-inf)
           if (lane == 0) defer_row(a, row);
         } else {
           int pos = incl - mine;
@@ -1999,6 +2002,11 @@ int launch_rowwarp(const KArgs &a, int nc, cudaStream_t st) {
   }
 }
 
+// Test hook: 0 = the usual choice, 1 = the stats + select pair, 3 = the
+// row-warp kernel, for batches that reach the choice between them (above the
+// small-batch path).
+std::atomic<int> g_force_path{0};
+
 template <bool BF16>
 int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
   const bool scalar_k = a.k_rows == nullptr;
@@ -2016,7 +2024,8 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
   if (a.N <= kSmallBatch && s.heads && s.rec_capacity >= a.N)
     return launch_small<BF16>(a, s, J, kcap, st);
   const int nc = rowwarp_nc<BF16>(a.V);
-  if (nc > 0 && (nc <= 9 || a.N <= kRowWarpMaxBatch)) {
+  const int force = g_force_path.load(std::memory_order_relaxed);
+  if (nc > 0 && (force == 3 || (force == 0 && (nc <= 9 || a.N <= kRowWarpMaxBatch)))) {
     const int rc = launch_rowwarp<BF16>(a, nc, st);
     if (rc != D3S_OK) return rc;
     return launch_wide<BF16>(a, 1, scalar_k ? kscalar : D3S_MAX_K, st);
@@ -2028,6 +2037,8 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
 }  // namespace
 
 int prepare_launch(const void *fn, int threads, size_t smem) { return prepare(fn, threads, smem); }
+
+void set_force_path(int path) { g_force_path.store(path, std::memory_order_relaxed); }
 
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t st) {
   if (a.N == 0) return D3S_OK;

@@ -79,6 +79,10 @@ struct Scratch {
 // blocks per SM for (threads, smem), cached; 0 when an attribute call failed.
 int prepare_launch(const void *fn, int threads, size_t smem);
 
+// Test hook: which kernel takes the batches above the small-batch path
+// (0 = the usual choice, 1 = stats + select pair, 3 = row-warp).
+void set_force_path(int path);
+
 // Launch the sampler for one request. Validates sizes; returns D3S_* status.
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t stream);
 

@@ -44,7 +44,8 @@ EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split"
            "d3s_lmhead_sample", "d3s_codes_write_npy", "d3s_static_check",
            "d3s_static_debug_set_error", "d3s_gather_create", "d3s_gather_export",
            "d3s_gather_attach", "d3s_gather_begin", "d3s_gather_end", "d3s_gather_release",
-           "d3s_gather_check", "d3s_gather_destroy", "d3s_gather_copy_result")
+           "d3s_gather_check", "d3s_gather_destroy", "d3s_gather_copy_result",
+           "d3s_debug_force_path")
 RAS_WINDOW = 16
 FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
 STATIC_MAX_ROWS = 4096
@@ -131,6 +132,7 @@ def lib() -> ctypes.CDLL:
         L.d3s_debug_math.argtypes = [vp, i32, vp, vp, i64, f32, vp]
         L.d3s_debug_div_check.argtypes = [vp, vp, i32, u64, u64, u64, vp, vp, vp]
         L.d3s_ctx_check.argtypes = [vp]
+        L.d3s_debug_force_path.argtypes = [i32]
         L.d3s_sample_rows_static.argtypes = [vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp]
         L.d3s_static_check.argtypes = [vp]
         L.d3s_gather_create.argtypes = [i32, i32, i32, i64, i32, ctypes.POINTER(vp)]
@@ -247,6 +249,14 @@ def sample(logits: np.ndarray, temperature, top_k, top_p, seed) -> np.ndarray:
     if rc not in (D3S_OK, D3S_ERR_NONFINITE):
         _check(rc)
     return out
+
+
+PATH_AUTO, PATH_PAIR, PATH_ROWWARP = 0, 1, 3
+
+
+def force_path(path: int) -> None:
+    """Test hook: the kernel for batches above the small-batch path (PATH_*)."""
+    _check(lib().d3s_debug_force_path(path))
 
 
 def last_status() -> int:

@@ -161,6 +161,13 @@ D3S_API int d3s_ctx_check(d3s_ctx *ctx);
  * special-function unit's 2^x that the approximate full-row sum uses. */
 D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_dev, int64_t n,
                            float param, void *stream);
+/* Test hook (no counterpart in the reference): which kernel samples the
+ * batches above the small-batch path (N > 512), process-wide: 0 = the usual
+ * choice, 1 = the streaming stats kernel + the select kernel, 3 = the
+ * row-warp kernel (one warp per row). A path that cannot take the request
+ * falls back to the usual one. Results are identical on every path; tests use
+ * it to check each of them. */
+D3S_API int d3s_debug_force_path(int path);
 /* Counts float bit patterns x in [lo, hi) (step `step`) with |x| in
  * [2^-100, 2^60], the reciprocal path's exact range, whose quotient x / T differs from the IEEE quotient, for each of
  * T_dev[nT]; adds to *bad_dev (device), last failing (x, T) in example_dev[2]. */

@@ -317,6 +317,33 @@ def c1_latency(ctx, torch):
     xs = synth.to_host_logits(synth.c1_rows(2000, seed=44))
     out.update(cpu_one_thread_row_us(xs, np.float32(0.7), np.float32(0.7), np.int32(30),
                                      np.uint64(42)))
+    # the same host-in, host-out call from C on both sides, without numpy work
+    # per call: the library's d3_sample and the oracle's, on preallocated arrays
+    import ctypes
+
+    import oracle
+    Lg, Lc = d3s.lib(), oracle.lib()
+    row = np.ascontiguousarray(xs[:1])
+    res = np.zeros(1, np.int32)
+    rp = row.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    op = res.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+
+    def p50(fn, n=1020):
+        ts = []
+        for i in range(n):
+            t0 = time.perf_counter()
+            fn(i)
+            ts.append((time.perf_counter() - t0) * 1e6)
+        ts = sorted(ts[20:])
+        return ts[len(ts) // 2], ts[int(len(ts) * 0.99)]
+
+    g50, g99 = p50(lambda i: Lg.d3_sample(rp, 1, row.shape[1], 0.7, 30, 0.7, i, op))
+    c50, c99 = p50(lambda i: Lc.d3o_d3_sample(rp, 1, row.shape[1], 0.7, 30, 0.7, i, op))
+    out.update({"c1_host_d3_sample_c_call_p50_us": g50, "c1_host_d3_sample_c_call_p99_us": g99,
+                "c1_cpu_1thread_c_call_p50_us": c50, "c1_cpu_1thread_c_call_p99_us": c99,
+                "c1_c_call_note": "ctypes calls of the C functions on preallocated arrays: the "
+                                  "library's d3_sample (host logits in, id out) and the oracle's "
+                                  "d3o_d3_sample on one host thread"})
     return out
 
 
@@ -392,6 +419,10 @@ def measure_c3(ctx, torch, B: int, steps: int, warmup: int):
         return statistics.mean(a.elapsed_time(b) for a, b in evs)
 
     proj_ms = timed(lambda: ctx.lmhead(h, W, out=logits))
+    # the practical ceiling for this transfer size: torch's own reduction reading
+    # the same weight bytes from HBM, timed the same way (a kernel this short is
+    # dominated by launch, first-touch latency and ramp, not by bandwidth)
+    read_ms = timed(lambda: torch.sum(W, dtype=torch.float32))
     fused_ms = timed(lambda: ctx.lmhead_sample(h, W, logits, ids, temperature=0.7, top_p=0.7,
                                                top_k=30, noise=d3s.NOISE_SEEDS, seeds=seeds))
     ctx.check()
@@ -414,6 +445,11 @@ def measure_c3(ctx, torch, B: int, steps: int, warmup: int):
                      {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s",
                       "frac": gbs / peak_gbs, "peak_source": gkind}),
         "hbm_gbs": gbs, "tflops": tfs, "bytes": bytes_, "flops": flops,
+        "calibration": {"torch_read_of_W_us": read_ms * 1e3,
+                        "torch_read_GBs": V * D * 2 / (read_ms / 1e3) / 1e9,
+                        "projection_vs_torch_read": read_ms / proj_ms,
+                        "note": "torch.sum over W's 16.8 MB after the same L2-clearing read: "
+                                "what a plain read of these bytes costs at this size"},
     }
 
 

@@ -3,6 +3,7 @@
 // (src/model.h:169-176, src/testapi.c:155-166). No entry point exits the
 // process; errors come back as D3S_ERR_* codes with a message.
 #include <algorithm>
+#include <climits>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -22,9 +23,12 @@ struct d3s_ctx {
   size_t stage_cap = 0;  // bytes
   cudaStream_t stream = nullptr;
   d3s::FrameScratch frame;  // d3s_frame_main's per-draw arrays
-  float *lm_ws = nullptr;   // d3s_lmhead's split-K partials
-  int64_t lm_ws_cap = 0;    // floats
   void *pinned = nullptr;   // d3_sample's host staging (stage_cap bytes), laid out as stage_dev
+  // d3_sample of one row: the logits and the result in pinned host memory
+  // mapped into the device, read and written by the kernel in place
+  unsigned char *row_host = nullptr;  // [logits | id, status]
+  unsigned char *row_dev = nullptr;   // the same bytes, device address
+  size_t row_cap = 0;                 // bytes
 };
 
 namespace {
@@ -316,10 +320,10 @@ void d3s_ctx_destroy(d3s_ctx *ctx) {
   cudaFree(ctx->scratch.counters);
   cudaFree(ctx->scratch.heads);
   cudaFree(ctx->scratch.cands);
+  cudaFreeHost(ctx->row_host);
   cudaFree(ctx->stage_dev);
   cudaFreeHost(ctx->pinned);
   cudaFree(ctx->frame.keys);
-  cudaFree(ctx->lm_ws);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -541,20 +545,6 @@ int d3s_lmhead(d3s_ctx *ctx, const void *h_dev, int64_t ld_h, const void *W_dev,
   a.out = logits_dev;
   a.ld_out = ld_logits;
   a.error = reinterpret_cast<int32_t *>(ctx->scratch.counters + 2);
-  const int64_t need = d3s::lmhead_workspace(B, V, D);
-  if (need > ctx->lm_ws_cap) {
-    float *w = nullptr;
-    const cudaError_t e = cudaMalloc(&w, (size_t)need * sizeof(float));
-    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "lm_head workspace: %s", cudaGetErrorString(e));
-    if (ctx->lm_ws) {
-      cudaDeviceSynchronize();  // queued projections may still use the old one
-      cudaFree(ctx->lm_ws);
-    }
-    ctx->lm_ws = w;
-    ctx->lm_ws_cap = need;
-  }
-  a.ws = ctx->lm_ws;
-  a.ws_cap = ctx->lm_ws_cap;
   rc = d3s::launch_lmhead(a, (cudaStream_t)stream);
   if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "lm_head launch");
   return D3S_OK;
@@ -588,6 +578,64 @@ static int default_ctx(d3s_ctx **out) {
   return D3S_OK;
 }
 
+// d3_sample of one row with the kernel reading the logits from, and writing
+// the id and status to, pinned host memory mapped into the device: no upload
+// or download, one launch and one synchronisation. Returns kHandedOn when the
+// kernel left the row on the hand-off list (k > 256 is excluded by the caller;
+// ties beyond the candidate list, fewer finite logits than k): the ordinary
+// path then samples it with the same subkey.
+constexpr int kHandedOn = 1;
+static int d3_sample_row(d3s_ctx *ctx, const float *logits, int V, float temperature, int top_k,
+                         float top_p, d3s_key sub, int *out) {
+  const size_t lbytes = ((size_t)V * sizeof(float) + 15) & ~(size_t)15;
+  const size_t need = lbytes + 16;
+  cudaError_t e;
+  if (need > ctx->row_cap) {
+    cudaStreamSynchronize(ctx->stream);  // the old buffer may be in use by queued work
+    cudaFreeHost(ctx->row_host);
+    ctx->row_host = ctx->row_dev = nullptr;
+    ctx->row_cap = 0;
+    e = cudaHostAlloc(reinterpret_cast<void **>(&ctx->row_host), need, cudaHostAllocMapped);
+    if (e != cudaSuccess) return fail(D3S_ERR_NOMEM, "mapped host staging: %s", cudaGetErrorString(e));
+    e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->row_dev), ctx->row_host, 0);
+    if (e != cudaSuccess) {
+      cudaFreeHost(ctx->row_host);
+      ctx->row_host = nullptr;
+      return cuda_fail(e, "cudaHostGetDevicePointer");
+    }
+    ctx->row_cap = need;
+  }
+  std::memcpy(ctx->row_host, logits, (size_t)V * sizeof(float));
+  volatile int32_t *res = reinterpret_cast<volatile int32_t *>(ctx->row_host + lbytes);
+  res[0] = INT32_MIN;  // stays when the row is handed on
+  res[1] = D3S_ROW_OK;
+  d3s_request r{};
+  r.logits = ctx->row_dev;
+  r.dtype = D3S_F32;
+  r.N = 1;
+  r.V = V;
+  r.ld = V;
+  r.temperature = temperature;
+  r.top_p = top_p;
+  r.top_k = top_k;
+  r.noise = D3S_NOISE_KEY;
+  r.key = sub;
+  r.ids = reinterpret_cast<int32_t *>(ctx->row_dev + lbytes);
+  r.status = r.ids + 1;
+  d3s::KArgs a = to_kargs(&r, ctx);
+  a.direct = 1;        // the kernel loads the mapped row itself (no waits, no error word)
+  a.skip_handoff = 1;  // a handed-on row is caught below
+  if (d3s::launch_sample(a, ctx->scratch, ctx->stream) != D3S_OK)
+    return cuda_fail(cudaGetLastError(), "sampler launch");
+  e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "d3_sample");
+  const int32_t id = res[0], st = res[1];
+  if (id == INT32_MIN) return kHandedOn;
+  out[0] = id;
+  if (st != D3S_ROW_OK) return fail(D3S_ERR_NONFINITE, "1 row(s) had non-finite logits");
+  return D3S_OK;
+}
+
 static int d3_sample_impl(const float *logits, int N, int V, float temperature, int top_k,
                           float top_p, unsigned long long seed, int *out) {
   if (N < 0 || V < 1 || (N > 0 && (!logits || !out))) return fail(D3S_ERR_ARG, "bad d3_sample args");
@@ -616,12 +664,23 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
   rc = check_request(&r);
   if (rc != D3S_OK) return rc;
   if (N == 0) return D3S_OK;
+  rc = reserve_scratch(ctx, N);
+  if (rc != D3S_OK) return rc;
+  d3s_seed(nullptr, seed);  // m_seed(seed), src/testapi.c:159
+  d3s_key sub;
+  take_subkey(nullptr, &sub);
+  // one row on the one-CTA kernel (V <= 8192, k <= 256): zero-copy
+  if (N == 1 && V <= 8192 && std::min(top_k, V) <= 256) {
+    rc = d3_sample_row(ctx, logits, V, temperature, top_k, top_p, sub, out);
+    if (rc != kHandedOn) return rc;
+  }
   // One staging layout on both sides: [logits | error word, pad | ids | status].
   // One copy uploads the logits with a zeroed error word, one brings the error
   // word, the ids and the statuses back.
   const size_t nl = (size_t)N * (size_t)V;
   const size_t tail = (nl * sizeof(float) + 15) & ~(size_t)15;
-  const size_t need = tail + 16 + 2 * (size_t)N * sizeof(int32_t);
+  const size_t down = 16 + 2 * (size_t)N * sizeof(int32_t);
+  const size_t need = tail + down;
   if (need > ctx->stage_cap) {
     cudaStreamSynchronize(ctx->stream);  // the old buffers may be in use by queued work
     cudaFree(ctx->stage_dev);
@@ -639,27 +698,21 @@ static int d3_sample_impl(const float *logits, int N, int V, float temperature, 
     }
     ctx->stage_cap = need;
   }
-  rc = reserve_scratch(ctx, N);
-  if (rc != D3S_OK) return rc;
   unsigned char *hp = static_cast<unsigned char *>(ctx->pinned);
   std::memcpy(hp, logits, nl * sizeof(float));
   std::memset(hp + nl * sizeof(float), 0, tail + 16 - nl * sizeof(float));
-  e = cudaMemcpyAsync(ctx->stage_dev, hp, tail + 16, cudaMemcpyHostToDevice, ctx->stream);
-  if (e != cudaSuccess) return cuda_fail(e, "logits upload");
   int32_t *ids_dev = reinterpret_cast<int32_t *>(ctx->stage_dev + tail + 16);
   r.logits = ctx->stage_dev;
   r.ids = ids_dev;
   r.status = ids_dev + N;
-  d3s_seed(nullptr, seed);  // m_seed(seed), src/testapi.c:159
-  d3s_key sub;
-  take_subkey(nullptr, &sub);
   r.key = sub;
   d3s::KArgs a = to_kargs(&r, ctx);
   a.error = reinterpret_cast<int32_t *>(ctx->stage_dev + tail);  // this call's own error word
-  rc = d3s::launch_sample(a, ctx->scratch, ctx->stream);
-  if (rc != D3S_OK) return cuda_fail(cudaGetLastError(), "sampler launch");
-  e = cudaMemcpyAsync(hp + tail, ctx->stage_dev + tail, 16 + 2 * (size_t)N * sizeof(int32_t),
-                      cudaMemcpyDeviceToHost, ctx->stream);
+  e = cudaMemcpyAsync(ctx->stage_dev, hp, tail + 16, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "logits upload");
+  if (d3s::launch_sample(a, ctx->scratch, ctx->stream) != D3S_OK)
+    return cuda_fail(cudaGetLastError(), "sampler launch");
+  e = cudaMemcpyAsync(hp + tail, ctx->stage_dev + tail, down, cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return cuda_fail(e, "d3_sample");
   const int32_t *h_err = reinterpret_cast<const int32_t *>(hp + tail);

@@ -715,11 +715,24 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
     fence_mbar_init();
   }
   __syncthreads();
-  if (t == 0)
+  const bool direct = SELECT && a.direct;
+  if (t == 0 && !direct)
     for (int s = 0; s < stages; ++s) {
       const int r = blockIdx.x + s * gridDim.x;
       if (r < a.N) issue_row<ESZ>(a, r, dsm + (size_t)s * span, &sm.mbar[s], pol);
     }
+  if (direct && (int)blockIdx.x < a.N) {
+    // the row lives in host memory mapped into the device: the CTA's threads
+    // copy its 16-byte-aligned span into the stage, each 16-byte load fetched
+    // anew from the host (ld.global.cv)
+    const uintptr_t start =
+        (uintptr_t)a.logits + (uintptr_t)phys_row(a, blockIdx.x) * (uintptr_t)a.ld * ESZ;
+    const uintptr_t lo = start & ~(uintptr_t)15;
+    const int chunks = (int)((((start + (uintptr_t)V * ESZ + 15) & ~(uintptr_t)15) - lo) / 16);
+    for (int c = t; c < chunks; c += NT)
+      reinterpret_cast<uint4 *>(dsm)[c] = __ldcv(reinterpret_cast<const uint4 *>(lo) + c);
+    __syncthreads();
+  }
   RawP nxt{};
   if (SELECT && (int)blockIdx.x < a.N) nxt = load_raw(a, blockIdx.x);
   // Persistent CTAs: each warp resolves the parameters of the CTA's next 32
@@ -761,7 +774,7 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       rp.k = __shfl_sync(kFull, k32, src);
     }
     const int s = it % stages, par = it & 1;
-    const bool ok = mbar_wait_bounded(&sm.mbar[s], (uint32_t)(it / stages) & 1u);
+    const bool ok = direct || mbar_wait_bounded(&sm.mbar[s], (uint32_t)(it / stages) & 1u);
     const unsigned char *rb =
         dsm + (size_t)s * span +
         (((uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ) & 15);
@@ -1958,6 +1971,7 @@ int launch_small(const KArgs &a, const Scratch &sc, int J, int wide_kcap, cudaSt
   if (prepare((const void *)fn, kFastThreads, smem) <= 0) return D3S_ERR_CUDA;
   fn<<<a.N, kFastThreads, smem, st>>>(a, sc.heads, sc.cands, 1, span);
   if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  if (a.skip_handoff) return D3S_OK;
   return launch_wide<BF16>(a, 1, wide_kcap, st, a.N);
 }
 
@@ -2043,6 +2057,13 @@ void set_force_path(int path) { g_force_path.store(path, std::memory_order_relax
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t st) {
   if (a.N == 0) return D3S_OK;
   return a.dtype == D3S_BF16 ? launch_typed<true>(a, s, st) : launch_typed<false>(a, s, st);
+}
+
+int launch_handoff(const KArgs &a, cudaStream_t st) {
+  if (a.N == 0) return D3S_OK;
+  const int kcap = a.k_rows ? D3S_MAX_K : std::min(a.top_k, a.V);
+  return a.dtype == D3S_BF16 ? launch_wide<true>(a, 1, kcap, st, a.N)
+                             : launch_wide<false>(a, 1, kcap, st, a.N);
 }
 
 int launch_uniform(uint2 key, int rows, int k, float *u, cudaStream_t st) {

@@ -41,6 +41,12 @@ struct KArgs {
   uint32_t *wide_done;
   int64_t deferred_cap;  // entries of `deferred`; hand-offs beyond it flag the row
   int32_t *error;        // set to 1 when a bounded wait gives up
+  // batches of one CTA per row: leave the rows handed on (no id written) on
+  // the list for a later launch_handoff instead of launching the wide kernel
+  int skip_handoff;
+  // batches of one CTA per row: the logits are host memory mapped into the
+  // device (zero-copy): each CTA loads its row with plain loads, no bulk copy
+  int direct;
   // the row-independent part of the approximate full-row sum's relative error
   // bound (set by the launcher of the approximate-sum kernels)
   float approx_c0;
@@ -85,6 +91,9 @@ void set_force_path(int path);
 
 // Launch the sampler for one request. Validates sizes; returns D3S_* status.
 int launch_sample(const KArgs &a, const Scratch &s, cudaStream_t stream);
+// The wide kernel over the hand-off list (rows a launch with skip_handoff left
+// there), on the same request.
+int launch_handoff(const KArgs &a, cudaStream_t stream);
 
 // One decode frame's main + retry draws for S streams (d3s_frame_request).
 struct FrameArgs {
@@ -121,12 +130,8 @@ struct LmArgs {
   void *out;
   int64_t ld_out;
   int32_t *error;  // bit 1 set when a bounded wait in the GEMM gave up
-  float *ws;       // split-K partials (device), lmhead_workspace() floats
-  int64_t ws_cap;
 };
 int launch_lmhead(const LmArgs &a, cudaStream_t stream);
-// fp32 workspace floats launch_lmhead needs for (B, V, D) on the current device
-int64_t lmhead_workspace(int B, int V, int D);
 
 // Advance S key states by n splits each; subkeys at sub[s * ld_sub + i].
 int launch_keys_next(uint2 *state, int S, int n, uint2 *sub, int64_t ld_sub, cudaStream_t stream);

@@ -14,7 +14,10 @@
 //     issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32 in TMEM) and commits
 //     each stage back to the producer; four epilogue warps read the
 //     accumulator with tcgen05.ld, round to bf16 and store logits[b, v].
-//     No clusters and no multicast: every CTA loads its own tiles.
+//     When the tiles alone leave most SMs idle (small B) the K loop is split
+//     over the CTAs of a cluster, whose fp32 partials are added on chip
+//     through distributed shared memory. No multicast: every CTA loads its own
+//     tiles.
 // Every wait on an mbarrier is bounded (kLmWaitLimitNs); a wait that gives up
 // sets the error word and the kernel drains its copies, frees its tensor
 // memory and returns.
@@ -151,12 +154,33 @@ struct GemmCfg {
   static_assert((kTmemCols & (kTmemCols - 1)) == 0, "TMEM columns: a power of two");
 };
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Float offset of (row, 16-byte chunk kc) in a [128][BN] fp32 partial whose
+// chunks are XOR-swizzled by row, so eight consecutive rows' same chunk fall
+// in eight different bank groups.
+template <int BN>
+__device__ __forceinline__ int part_off(int row, int kc) {
+  return row * BN + 4 * (kc ^ (row & 7));
+}
+
+// ks > 1: the ks CTAs of a cluster (along z) split the K loop of one output
+// tile; once every CTA's MMAs are complete (a cluster barrier), the CTAs of
+// rank > 0 store their fp32 partials into the rank-0 CTA's shared memory (its
+// stages, free by then) through distributed shared memory, and after a second
+// cluster barrier rank 0 adds them in rank order and writes bf16 logits.
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     lmhead_gemm_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmH, __nv_bfloat16 *out,
-                       int64_t ld_out, int V, int B, int KT, int kps, float *ws,
-                       int32_t *error) {
+                       int64_t ld_out, int V, int B, int KT, int kps, int ks, int32_t *error) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ unsigned char dsmem[];
@@ -170,7 +194,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kBM;  // first W row (logit id) of the tile
   const int n0 = blockIdx.y * BN;   // first batch row of the tile
-  // split K: this CTA's k-tiles [kt0, kt0 + nk); its partial goes to ws
+  // split K: this CTA's k-tiles [kt0, kt0 + nk)
   const int kt0 = blockIdx.z * kps;
   const int nk = min(KT - kt0, kps);
 
@@ -242,19 +266,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool ok = bar_wait(accum, 0, abort_flag);
     tc_fence_after();
     const int v = m0 + q * 32 + lane;
+    if (ks == 1) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
-      if (ok && !*abort_flag && v < V) {
-        if (ws) {  // split K: the fp32 partial of this CTA's k-tiles
-          float *wz = ws + (size_t)blockIdx.z * B * V;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int b = n0 + c + j;
-            if (b < B) wz[(size_t)b * V + v] = __uint_as_float(r[j]);
-          }
-        } else {
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+        if (ok && !*abort_flag && v < V) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int b = n0 + c + j;
@@ -263,8 +280,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
-    tc_fence_before();
   }
+  if (ks > 1) {
+    // every CTA of the cluster has its partial in TMEM and its stages free
+    cluster_sync_all();
+    const uint32_t rank = cluster_rank();
+    float *part = reinterpret_cast<float *>(base);  // [ks - 1][128][BN] in rank 0's stages
+    if (warp >= 2 && rank > 0) {
+      const int q = warp & 3, row = q * 32 + lane;
+      float *mine = part + (size_t)(rank - 1) * kBM * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const uint32_t local = saddr(mine + part_off<BN>(row, (c + j) >> 2));
+          uint32_t remote;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(local));
+          asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(remote),
+                       "r"(r[j]), "r"(r[j + 1]), "r"(r[j + 2]), "r"(r[j + 3])
+                       : "memory");
+        }
+      }
+    }
+    cluster_sync_all();  // the partials are in rank 0's shared memory
+    if (warp >= 2 && rank == 0) {
+      const int q = warp & 3, row = q * 32 + lane, v = m0 + row;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
+        for (int z = 1; z < ks; ++z) {  // rank order: the sum of the k-tiles in split order
+          const float *pz = part + (size_t)(z - 1) * kBM * BN;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(pz + part_off<BN>(row, (c + j) >> 2));
+            acc[j] = __fadd_rn(acc[j], f.x);
+            acc[j + 1] = __fadd_rn(acc[j + 1], f.y);
+            acc[j + 2] = __fadd_rn(acc[j + 2], f.z);
+            acc[j + 3] = __fadd_rn(acc[j + 3], f.w);
+          }
+        }
+        if (!*abort_flag && v < V) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int b = n0 + c + j;
+            if (b < B) out[(int64_t)b * ld_out + v] = __float2bfloat16_rn(acc[j]);
+          }
+        }
+      }
+    }
+  }
+  if (warp >= 2) tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -273,18 +344,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                  : "memory");
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(error, 2);
-}
-
-// Split-K sum: out[b, v] = bf16(ws[0][b][v] + ws[1][b][v] + ...), in split order.
-__global__ void lmhead_reduce_kernel(const float *ws, int KS, int B, int V, __nv_bfloat16 *out,
-                                     int64_t ld_out) {
-  const size_t n = (size_t)B * V, stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    float acc = ws[i];
-    for (int z = 1; z < KS; ++z) acc = __fadd_rn(acc, ws[(size_t)z * n + i]);
-    const size_t b = i / (size_t)V, v = i - b * (size_t)V;
-    out[(int64_t)b * ld_out + (int64_t)v] = __float2bfloat16_rn(acc);
-  }
 }
 
 // ---- 2-SM GEMM (B >= 256): a CTA pair shares one 256 x 256 UMMA tile ----
@@ -305,15 +364,6 @@ constexpr uint32_t kHalfBytes = 128 * kBK * 2;        // 128 rows x 64 k of bf16
 constexpr uint32_t kStageBytes2 = 2 * kHalfBytes;     // this CTA's W half + h half
 constexpr size_t kSmem2 = (size_t)kStages2 * kStageBytes2 + (2 * kStages2 + 1) * 8 + 16 + 1024;
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
 // shared::cluster address of the same object in CTA `rank` of the cluster
 __device__ __forceinline__ uint32_t peer_addr(const void *p, uint32_t rank) {
   uint32_t r;
@@ -601,17 +651,38 @@ int sm_count() {
   return sms;
 }
 
-int gemm_bn(int B) { return B <= 32 ? 32 : (B <= 64 ? 64 : (B <= 128 ? 128 : 256)); }
-
 // Split K when the output tiles leave most SMs idle (small B): about one CTA
-// per SM, at least four k-tiles per split.
-void gemm_splits(int B, int V, int D, int BN, int &kps, int &KS) {
+// per SM, at least four k-tiles per split, and (the splits of a tile being one
+// cluster) no more clusters than fit on the GPU at once.
+template <int BN>
+int gemm_splits(int B, int V, int D, int &kps) {
   const int KT = (D + kBK - 1) / kBK;
   const int tiles = ((V + kBM - 1) / kBM) * ((B + BN - 1) / BN);
   int want = std::max(1, std::min(8, sm_count() / std::max(tiles, 1)));
   want = std::min(want, std::max(1, KT / 4));
+  // the partials of ranks 1 .. want - 1 must fit in rank 0's stages
+  const size_t part_bytes = (size_t)kBM * BN * 4;
+  want = std::min(want, 1 + (int)((size_t)GemmCfg<BN>::kStages * GemmCfg<BN>::kStageBytes / part_bytes));
+  for (; want > 1; --want) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((V + kBM - 1) / kBM, (B + BN - 1) / BN, want);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = GemmCfg<BN>::kSmem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = (unsigned)want;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, lmhead_gemm_kernel<BN>, &cfg) == cudaSuccess &&
+        clusters >= tiles)
+      break;
+    cudaGetLastError();  // a refused query is not an error of the launch
+  }
   kps = (KT + want - 1) / want;
-  KS = (KT + kps - 1) / kps;
+  return (KT + kps - 1) / kps;
 }
 
 template <int BN>
@@ -623,20 +694,25 @@ int launch_gemm(const LmArgs &a, cudaStream_t st) {
   if (prepare_launch((const void *)lmhead_gemm_kernel<BN>, kGemmThreads, Cfg::kSmem) <= 0)
     return D3S_ERR_CUDA;
   const int KT = (a.D + kBK - 1) / kBK;
-  int kps = KT, KS = 1;
-  gemm_splits(a.B, a.V, a.D, BN, kps, KS);
-  if (KS > 1 && (!a.ws || a.ws_cap < (int64_t)KS * a.B * a.V)) return D3S_ERR_ARG;
-  const dim3 grid((a.V + kBM - 1) / kBM, (a.B + BN - 1) / BN, KS);
+  int kps = KT;
+  const int KS = gemm_splits<BN>(a.B, a.V, a.D, kps);
+  if ((size_t)(KS - 1) * kBM * BN * 4 > (size_t)Cfg::kStages * Cfg::kStageBytes) return D3S_ERR_ARG;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.V + kBM - 1) / kBM, (a.B + BN - 1) / BN, KS);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = (unsigned)KS;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
   __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(a.out);
-  lmhead_gemm_kernel<BN><<<grid, kGemmThreads, Cfg::kSmem, st>>>(
-      tw, th, out, a.ld_out, a.V, a.B, KT, kps, KS > 1 ? a.ws : nullptr, a.error);
-  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
-  if (KS > 1) {
-    const size_t n = (size_t)a.B * a.V;
-    const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
-    lmhead_reduce_kernel<<<blocks, 256, 0, st>>>(a.ws, KS, a.B, a.V, out, a.ld_out);
-  }
-  return cudaGetLastError() == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, lmhead_gemm_kernel<BN>, tw, th, out, a.ld_out,
+                                           a.V, a.B, KT, kps, KS, a.error);
+  return e == cudaSuccess ? D3S_OK : D3S_ERR_CUDA;
 }
 
 int launch_gemm2(const LmArgs &a, cudaStream_t st) {
@@ -673,13 +749,6 @@ int launch_gemv(const LmArgs &a, cudaStream_t st) {
 }
 
 }  // namespace
-
-int64_t lmhead_workspace(int B, int V, int D) {
-  if (B <= kGemvMaxB || B >= kPairMinB) return 0;
-  int kps, KS;
-  gemm_splits(B, V, D, gemm_bn(B), kps, KS);
-  return KS > 1 ? (int64_t)KS * B * V : 0;
-}
 
 int launch_lmhead(const LmArgs &a, cudaStream_t st) {
   if (a.B == 0 || a.V == 0) return D3S_OK;

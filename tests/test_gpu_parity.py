@@ -136,6 +136,37 @@ def test_d3_sample_status_follows_each_call(oracle):
     assert d3s.last_status() == d3s.D3S_OK
 
 
+def test_d3_sample_one_row_zero_copy_path(oracle):
+    """One-row d3_sample calls run the one-CTA kernel on logits in mapped host
+    memory and write the id there: every call equals the oracle across seeds,
+    parameters and changes of V and top_k, a non-finite row is flagged, a row
+    with fewer finite logits than k is handed on to the ordinary path, and a
+    large call in between (the context's scratch regrown) changes nothing."""
+    import d3s
+    rng = np.random.default_rng(77)
+    for V, k in [(4097, 30), (4097, 30), (1024, 5), (4097, 64), (4097, 30)]:
+        x = (rng.standard_normal((24, V)) * 3).astype(np.float32)
+        for i in range(24):
+            T, p = float(rng.uniform(0.5, 1.2)), float(rng.uniform(0.5, 1.0))
+            got = d3s.sample(x[i:i + 1], T, k, p, 1000 * V + i)
+            assert d3s.last_status() == d3s.D3S_OK
+            assert got.tolist() == oracle.d3_sample(x[i:i + 1], T, k, p, 1000 * V + i).tolist()
+        bad = x[:1].copy()
+        bad[0, 11] = np.inf
+        assert d3s.sample(bad, 0.7, k, 0.7, 5).tolist() == [-1]
+        assert d3s.last_status() == d3s.D3S_ERR_NONFINITE
+        # a row with fewer finite logits than k is handed to the wide kernel
+        masked = np.full((1, V), -np.inf, np.float32)
+        masked[0, :3] = x[0, :3]
+        assert d3s.sample(masked, 0.7, k, 0.9, 6).tolist() == oracle.d3_sample(masked, 0.7, k, 0.9, 6).tolist()
+        assert d3s.last_status() == d3s.D3S_OK
+    big = (rng.standard_normal((3000, 300)) * 3).astype(np.float32)
+    assert d3s.sample(big, 0.8, 20, 0.9, 9).tolist() == oracle.d3_sample(big, 0.8, 20, 0.9, 9).tolist()
+    one = (rng.standard_normal((1, 4097)) * 3).astype(np.float32)
+    for s_ in range(5):
+        assert d3s.sample(one, 0.7, 30, 0.7, s_).tolist() == oracle.d3_sample(one, 0.7, 30, 0.7, s_).tolist()
+
+
 def test_config1_ten_thousand_sequential_draws(ctx, oracle, synth):
     """Config 1 as the reference's CLI runs it: m_seed(42) once
     (src/main.c:195), then 10,000 sequential sample_top_k_top_p calls on the

@@ -87,3 +87,30 @@ def test_no_cpu_fallback_without_gpu():
     assert (ids == -1).all()
     with pytest.raises(d3s.D3SError):
         d3s.Context(0)
+
+
+def test_new_entry_points_check_their_arguments_before_any_device_work():
+    """Argument errors come back as codes without touching a device: the
+    allocation-free entry point's row limit, the gather's world / rank / slots,
+    and the kernel-path test hook's range."""
+    import d3s
+    L = d3s.lib()
+    vp = ctypes.c_void_p
+    rc = L.d3s_sample_rows_static(vp(16), d3s.F32, d3s.STATIC_MAX_ROWS + 1, 8, 8, vp(16), vp(16),
+                                  vp(16), vp(16), vp(16), None)
+    assert rc == d3s.D3S_ERR_UNSUPPORTED
+    assert L.d3s_sample_rows_static(None, d3s.F32, -1, 8, 8, None, None, None, None, None,
+                                    None) == d3s.D3S_ERR_ARG
+    assert L.d3s_sample_rows_static(None, 7, 1, 8, 8, None, None, None, None, None,
+                                    None) == d3s.D3S_ERR_ARG
+    assert L.d3s_sample_rows_static(None, d3s.F32, 0, 8, 8, None, None, None, None, None,
+                                    None) == d3s.D3S_OK
+    g = vp()
+    for world, rank, rows, slots in [(0, 0, 8, 2), (2, 2, 8, 2), (2, -1, 8, 2), (2, 0, -1, 2),
+                                     (2, 0, 8, 1), (2, 0, 8, 65)]:
+        assert L.d3s_gather_create(0, world, rank, rows, slots, ctypes.byref(g)) == d3s.D3S_ERR_ARG
+        assert not g.value
+    for bad in (-1, 4, 100):
+        with pytest.raises(d3s.D3SError):
+            d3s.force_path(bad)
+    d3s.force_path(d3s.PATH_AUTO)

@@ -89,7 +89,7 @@ def load_traffic():
 
 class Clocks:
     """SM clocks and clock-event (throttle) reasons sampled through NVML every
-    millisecond or so while the timed region runs (read-only queries)."""
+    quarter millisecond or so while the timed region runs (read-only queries)."""
 
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
                0x4: "sw_power_cap"}
@@ -614,7 +614,7 @@ def run_ours(args):
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").replace(",", "").isdigit() else local
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
-    with Clocks(uuid, phys, 0.001 if rank == 0 else 0.002) as clk:
+    with Clocks(uuid, phys, 0.00025 if rank == 0 else 0.001) as clk:
         start.record(st)
         for i in range(args.steps):
             out = target()

@@ -424,7 +424,8 @@ int d3s_debug_div_check(d3s_ctx *ctx, const float *T_dev, int nT, uint64_t lo, u
 }
 
 int d3s_debug_force_path(int path) {
-  if (path != 0 && path != 1 && path != 3) return fail(D3S_ERR_ARG, "path %d not 0, 1 or 3", path);
+  if (path != 0 && path != 1 && path != 3 && path != 4)
+    return fail(D3S_ERR_ARG, "path %d not 0, 1, 3 or 4", path);
   d3s::set_force_path(path);
   return D3S_OK;
 }

@@ -1582,6 +1582,354 @@ __global__ void __launch_bounds__(32, RwBounds<NC>::kMinBlocks)
   }
 }
 
+// ---- one-warp stats kernel: the streaming pass with one warp per row ----
+//
+// The approximate-sum stats of the pair, done by one warp per row instead of
+// four, so the per-row work (parameters, reductions, threshold, sums,
+// candidate positions) runs once per row. Warp gw of the grid (NW warps) takes
+// rows gw, gw + NW, ...; it owns `depth` stages of NC * 512 bytes (every chunk a
+// lane reads) and keeps the bulk copies of its next depth - 1 rows in flight.
+// Per row:
+//   the stage's elements outside the row (before it in the first chunk, after
+//     it up to the end of the stage) are set to -inf, so no pass tests bounds;
+//   pass 1: lane l reads 16-byte chunks l + 32 i; each chunk's max stays in a
+//     register, chunk i also feeds group i % 4's max; the row max;
+//   threshold: for each group the ceil(k/4)-th largest of its 32 lane maxima
+//     (repeated warp max reduxes), then the largest of the four that at least
+//     k of the 128 group maxima reach (each such maximum is a distinct element,
+//     and the smallest of the four always qualifies); tau_lo just under it as
+//     in the four-warp kernel;
+//   pass 2: the terms 2^(x c + g) by the SFU into eight accumulators and one
+//     candidate bit per chunk (chunk max > tau_lo);
+//   the candidates (x > tau_lo) of the chunks whose bit is set into the row's
+//     list at positions from a shared counter (their order does not matter:
+//     the select kernel ranks them by key);
+//   the header, then the bulk copy of row it + depth into the stage.
+// Rows the approximate path does not take (k > 128, T or |x| at the extremes)
+// go to the wide kernel; bad parameters and non-finite rows are flagged here.
+// The exact stats of a row in the one-warp kernel's stage (rows with k <= 256
+// that the approximate path does not take): the row min, the candidate
+// threshold (min over eight groups, chunk i in group i % 8, of the
+// ceil(k/8)-th largest of the 32 lanes' group maxima, so at least k elements
+// reach it), then the definition's 256 partial sums as the row-warp kernel
+// computes them (lane l holds partials 4l + e - s + 128 (i & 1) of f32 rows,
+// 8l + e - s of bf16 rows, each a sequential float sum in element order; q by
+// the per-row reciprocal where that is the IEEE quotient; exp with the -86
+// floor; padding adds +0) and every element with q >= RN(taux / T) into the
+// row's list. Returns the fixed-point full-row sum. Loops stay rolled: such
+// rows are rare, and the code must not crowd the approximate path.
+template <int NC, bool BF16>
+__device__ __forceinline__ unsigned long long stats1_exact(const KArgs &a, const RowP &rp, RowCands &Cs,
+                                                           const unsigned char *stage, unsigned *cand_n,
+                                                           float xmax, float gmax, float rT, int s,
+                                                           int lane) {
+  constexpr int EPC = BF16 ? 8 : 4;
+  const int V = a.V;
+  float mn = f_inf(), v8[8], t8[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) v8[g] = -f_inf();
+#pragma unroll 1
+  for (int i8 = 0; i8 < NC; i8 += 8) {
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      const int ch = lane + 32 * (i8 + h);
+      if (i8 + h < NC) {
+        float x[EPC];
+        rw_chunk<BF16>(stage, ch, x);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+          const int p = EPC * ch + e;
+          mn = fminf(mn, (p >= s && p < V + s) ? x[e] : f_inf());
+          v8[h] = fmaxf(v8[h], x[e]);  // outside the row the stage holds -inf
+        }
+      }
+    }
+  }
+  const float xmin = -warp_max(-mn);
+  const int r = (rp.k + 7) >> 3;  // <= 32: k <= 256
+  for (int j = 0;; ++j) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g) t8[g] = warp_max(v8[g]);
+    if (j + 1 >= r) break;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) v8[g] = v8[g] == t8[g] ? -f_inf() : v8[g];
+  }
+  float taux = t8[0];
+#pragma unroll
+  for (int g = 1; g < 8; ++g) taux = fminf(taux, t8[g]);
+  const float T = rp.T;
+  const float tau = __fdiv_rn(taux, T);
+  const bool fast = div_rows_ok(xmin, xmax, T, gmax, tau);
+  float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                   make_float2(0.0f, 0.0f)};
+#pragma unroll 1
+  for (int i2 = 0; i2 < NC; i2 += 2) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int ch = lane + 32 * (i2 + h);
+      if (i2 + h < NC) {
+        float x[EPC];
+        rw_chunk<BF16>(stage, ch, x);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+          const int p = EPC * ch + e;
+          const bool valid = p >= s && p < V + s;
+          const float q = fast ? div_rows(x[e], rT, -T) : __fdiv_rn(x[e], T);
+          const float t = valid ? exp_term(__fsub_rn(q, gmax)) : 0.0f;
+          const int ai = BF16 ? e / 2 : 2 * h + e / 2;
+          if (e & 1)
+            acc[ai].y = __fadd_rn(acc[ai].y, t);
+          else
+            acc[ai].x = __fadd_rn(acc[ai].x, t);
+          if (valid && q >= tau) {
+            const unsigned pos = atomicAdd(cand_n, 1u);
+            if (pos < (unsigned)kCandCap) Cs.cand[pos] = raw_cand(x[e], (uint32_t)(p - s));
+          }
+        }
+      }
+    }
+  }
+  unsigned long long fx = 0ull;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    fx += __float2ull_rz(__fmul_rn(acc[j].x, 0x1p46f)) + __float2ull_rz(__fmul_rn(acc[j].y, 0x1p46f));
+  return warp_sum_u64(fx);
+}
+
+constexpr int kS1MaxWarps = 16;
+constexpr int kS1MaxDepth = 4;
+constexpr int kS1SmemBytes = 227 * 1024 - 1024;  // dynamic shared memory of the one-warp kernel's CTA
+
+template <int NC, bool BF16>
+__global__ void __launch_bounds__(32 * kS1MaxWarps)
+    sample_stats1_kernel(const KArgs a, RowHead *heads, RowCands *cands, int depth) {
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ uint64_t bars[kS1MaxWarps][kS1MaxDepth];
+  __shared__ unsigned cand_n[kS1MaxWarps];
+  constexpr int ESZ = BF16 ? 2 : 4;
+  constexpr int EPC = 16 / ESZ;
+  constexpr int SB = NC * 512;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int nwb = blockDim.x >> 5;
+  const int V = a.V;
+  unsigned char *stages = dsm + (size_t)w * depth * SB;
+  uint64_t *bar = bars[w];
+  const uint64_t pol = evict_first_policy();
+  const long long gw = (long long)blockIdx.x * nwb + w, NW = (long long)gridDim.x * nwb;
+  if (lane == 0) {
+    for (int d = 0; d < depth; ++d) mbar_init(&bar[d], 1);
+    cand_n[w] = 0u;
+    fence_mbar_init();
+    for (int d = 0; d < depth; ++d)
+      if (gw + d * NW < a.N) issue_row<ESZ>(a, (int)(gw + d * NW), stages + (size_t)d * SB, &bar[d], pol);
+  }
+  __syncwarp();
+  float T32 = 1.0f, c32 = 1.0f, rT32 = 1.0f;
+  int k32 = 1, st32 = D3S_ROW_BADPARAM;
+  int slot = 0;
+  uint32_t phase = 0u;
+  int it = 0;
+  bool failed = false;
+  for (;; ++it) {
+    const long long row64 = gw + (long long)it * NW;
+    if (row64 >= a.N) break;
+    const int row = (int)row64;
+    // the parameters of the warp's next 32 rows, lane i those of the i-th
+    if ((it & 31) == 0) {
+      const long long r = row64 + (long long)lane * NW;
+      if (r < a.N) {
+        RowP q{1.0f, 1.0f, 1};
+        st32 = resolve(a, load_raw(a, (int)r), q);
+        T32 = q.T;
+        k32 = q.k;
+        c32 = __fdiv_rn(kL2E, q.T);
+        rT32 = __frcp_rn(q.T);
+      }
+    }
+    const int src = it & 31;
+    const int pst = __shfl_sync(kFull, st32, src);
+    RowP rp;
+    rp.T = __shfl_sync(kFull, T32, src);
+    rp.k = __shfl_sync(kFull, k32, src);
+    rp.p = 1.0f;
+    const float c = __shfl_sync(kFull, c32, src), rT = __shfl_sync(kFull, rT32, src);
+    unsigned char *stage = stages + (size_t)slot * SB;
+    if (!__all_sync(kFull, mbar_wait_bounded(&bar[slot], phase))) {
+      failed = true;
+      break;
+    }
+    const uintptr_t start =
+        (uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ;
+    const int s = (int)((start & 15) / ESZ);
+    const int nch = (int)((((start + (uintptr_t)V * ESZ + 15) & ~(uintptr_t)15) - (start & ~(uintptr_t)15)) / 16);
+    // -inf outside the row: the s elements before it, the rest of its last
+    // chunk, and every chunk past the copy up to the end of the stage
+    if constexpr (BF16) {
+      unsigned short *e = reinterpret_cast<unsigned short *>(stage);
+      if (lane < s) e[lane] = 0xFF80u;
+      if (V + s + lane < nch * EPC && lane < EPC) e[V + s + lane] = 0xFF80u;
+    } else {
+      float *e = reinterpret_cast<float *>(stage);
+      if (lane < s) e[lane] = -f_inf();
+      if (V + s + lane < nch * EPC && lane < EPC) e[V + s + lane] = -f_inf();
+    }
+    {
+      const uint4 ninf = BF16 ? make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u)
+                              : make_uint4(0xFF800000u, 0xFF800000u, 0xFF800000u, 0xFF800000u);
+      for (int ch = nch + lane; ch < 32 * NC; ch += 32) reinterpret_cast<uint4 *>(stage)[ch] = ninf;
+    }
+    __syncwarp();
+
+    // pass 1: chunk maxima, group maxima, the row max
+    float cm[NC];
+    float gm[4] = {-f_inf(), -f_inf(), -f_inf(), -f_inf()};
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      float x[EPC];
+      rw_chunk<BF16>(stage, lane + 32 * i, x);
+      float m = max_nan(x[0], x[1]);
+#pragma unroll
+      for (int e = 2; e < EPC; e += 2) m = max_nan(m, max_nan(x[e], x[e + 1]));
+      cm[i] = m;
+      gm[i & 3] = max_nan(gm[i & 3], m);
+    }
+    const float xmax = warp_max_nan(max_nan(max_nan(gm[0], gm[1]), max_nan(gm[2], gm[3])));
+
+    RowHead &H = heads[row];
+    // 0: written here (flagged or handed on), 1: approximate stats, 2: exact stats
+    int mode = 0;
+    float gmax = 0.0f, taux = 0.0f;
+    if (pst != D3S_ROW_OK) {
+      if (lane == 0) flag_row(a, row, pst);
+    } else if (rp.k > kFastMaxK) {
+      if (lane == 0) defer_row(a, row);
+    } else {
+      const float ax = fabsf(xmax);
+      gmax = (ax >= 0x1p-100f && ax <= 0x1p60f && rp.T >= 0x1p-17f && rp.T <= 0x1p20f)
+                 ? div_rows(xmax, rT, -rp.T)
+                 : __fdiv_rn(xmax, rp.T);  // max(x / T) = RN(max(x) / T): RN is monotone
+      if (!(fabsf(gmax) < f_inf())) {     // NaN, +inf, or every value -inf
+        if (lane == 0) flag_row(a, row, D3S_ROW_NONFINITE);
+      } else if (rp.k <= kApproxMaxK) {
+        const int r = (rp.k + 3) >> 2;  // <= 32
+        float v[4] = {gm[0], gm[1], gm[2], gm[3]}, t[4];
+        for (int j = 0;; ++j) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) t[g] = warp_max(v[g]);
+          if (j + 1 >= r) break;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) v[g] = v[g] == t[g] ? -f_inf() : v[g];
+        }
+        taux = fminf(fminf(t[0], t[1]), fminf(t[2], t[3]));
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          int n = 0;
+#pragma unroll
+          for (int h = 0; h < 4; ++h) n += gm[h] >= t[g] ? 1 : 0;
+          if ((int)__reduce_add_sync(kFull, (unsigned)n) >= rp.k) taux = fmaxf(taux, t[g]);
+        }
+        mode = approx_row_ok(rp, xmax, taux) ? 1 : 2;
+      } else {
+        mode = 2;
+      }
+    }
+    if (mode == 0) {
+      if (lane == 0) H.done = 1;
+    } else {
+      RowCands &Cs = cands[row];
+      unsigned long long S;
+      if (mode == 1) {
+        // pass 2: the approximate full-row sum and the candidate chunks
+        const float tau_lo = __fmaf_rn(-fabsf(taux), 0x1p-21f, taux);
+        const float2 c2 = make_float2(c, c);
+        const float g = __fmul_rn(-xmax, c);
+        const float2 g2 = make_float2(g, g);
+        float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                         make_float2(0.0f, 0.0f)};
+        uint32_t b0 = 0u, b1 = 0u;  // bit i: chunk i (i < 32), chunk 32 + i
+#pragma unroll
+        for (int i = NC - 1; i >= 0; --i) {
+          float x[EPC];
+          rw_chunk<BF16>(stage, lane + 32 * i, x);
+#pragma unroll
+          for (int pp = 0; pp < EPC / 2; ++pp) {
+            const float2 u = __ffma2_rn(make_float2(x[2 * pp], x[2 * pp + 1]), c2, g2);
+            const int ai = (2 * i + pp) & 3;
+            acc[ai] = __fadd2_rn(acc[ai], make_float2(ex2_approx(u.x), ex2_approx(u.y)));
+          }
+          // the sign of tau_lo - max: set when the chunk holds an element > tau_lo
+          const uint32_t d = __float_as_uint(__fsub_rn(tau_lo, cm[i]));
+          if (i >= 32)
+            b1 = __funnelshift_l(d, b1, 1);
+          else
+            b0 = __funnelshift_l(d, b0, 1);
+        }
+        const float2 s4 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+        S = warp_sum_u64(__float2ull_rz(__fmul_rn(__fadd_rn(s4.x, s4.y), 0x1p46f)));
+        // the candidates of the marked chunks
+        while (__any_sync(kFull, (b0 | b1) != 0u)) {
+          if ((b0 | b1) != 0u) {
+            int i;
+            if (b0) {
+              i = __ffs(b0) - 1;
+              b0 &= b0 - 1;
+            } else {
+              i = 32 + __ffs(b1) - 1;
+              b1 &= b1 - 1;
+            }
+            const int ch = lane + 32 * i;
+            float x[EPC];
+            rw_chunk<BF16>(stage, ch, x);
+            int n = 0;
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) n += x[e] > tau_lo ? 1 : 0;
+            unsigned pos = atomicAdd(&cand_n[w], (unsigned)n);
+#pragma unroll
+            for (int e = 0; e < EPC; ++e)
+              if (x[e] > tau_lo) {
+                if (pos < (unsigned)kCandCap) Cs.cand[pos] = raw_cand(x[e], (uint32_t)(EPC * ch + e - s));
+                ++pos;
+              }
+          }
+        }
+      } else {
+        S = stats1_exact<NC, BF16>(a, rp, Cs, stage, &cand_n[w], xmax, gmax, rT, s, lane);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const int C = (int)atomicExch(&cand_n[w], 0u);
+        reinterpret_cast<int4 *>(&H)[0] = make_int4(__float_as_int(gmax), 0, C, mode == 1 ? 1 : 0);
+        reinterpret_cast<ulonglong2 *>(&H)[1] = make_ulonglong2(S, 0ull);
+        reinterpret_cast<ulonglong2 *>(&H)[2] = make_ulonglong2(0ull, 0ull);
+      }
+    }
+    // the stage has been read: the copy of row it + depth goes into it
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      const long long nrow = row64 + (long long)depth * NW;
+      if (nrow < a.N) issue_row<ESZ>(a, (int)nrow, stage, &bar[slot], pol);
+    }
+    if (++slot == depth) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+  if (failed && lane == 0) {
+    // A bulk copy did not complete in time: record it, then wait (bounded) for
+    // this warp's copies still in flight before the shared memory goes away.
+    atomicOr(a.error, 1);
+    for (int d = 0; d < depth; ++d) {
+      if (gw + (long long)(it + d) * NW >= a.N) break;
+      if (!mbar_wait_bounded(&bar[slot], phase)) break;
+      if (++slot == depth) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+}
+
 // ---- wide kernel ----
 
 // Rows on the hand-off list are processed in full (exact max, exact full-row
@@ -1958,6 +2306,46 @@ int launch_fast(const KArgs &a0, const Scratch &sc, int J, int wide_kcap, cudaSt
   return launch_wide<BF16>(a, 1, wide_kcap, st, 1 << 30, sc.heads, sc.cands);
 }
 
+// The pair with the one-warp stats kernel: stats1 -> select -> wide kernel.
+template <bool BF16, int NC>
+int launch_fast1_nc(const KArgs &a0, const Scratch &sc, int wide_kcap, cudaStream_t st) {
+  KArgs a = a0;
+  // longest sequential chain of the approximate sum: a float of an accumulator
+  // takes one term per chunk of its parity (f32) or per chunk (bf16), then
+  // three levels of the final adds
+  a.approx_c0 = approx_bound_c0(a.V, (BF16 ? NC : (NC + 1) / 2) + 3);
+  // one stage a warp (the copy of a warp's next row starts when it has read
+  // its row), as many warps as one CTA's shared memory holds stages: the pass
+  // is bound by rows in flight, and warps running rows are worth more than
+  // rows copied ahead
+  const int depth = 1;
+  const int warps = std::min(kS1MaxWarps, std::max(1, (int)((kS1SmemBytes) / (NC * 512))));
+  const size_t smem = (size_t)warps * depth * NC * 512;
+  auto fn = sample_stats1_kernel<NC, BF16>;
+  const int occ = prepare((const void *)fn, 32 * warps, smem, true);
+  const int sms = device_sms();
+  if (occ <= 0 || sms <= 0) return D3S_ERR_CUDA;
+  const long long need = (a.N + warps - 1) / warps;
+  const int grid = (int)std::max(1LL, std::min(need, (long long)sms * occ));
+  fn<<<grid, 32 * warps, smem, st>>>(a, sc.heads, sc.cands, depth);
+  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  const int sel_occ = prepare((const void *)sample_select_kernel, kSelThreads, 0);
+  const int sel_grid = std::max(1, std::min((a.N + kSelWarps - 1) / kSelWarps, sms * sel_occ));
+  sample_select_kernel<<<sel_grid, kSelThreads, 0, st>>>(a, sc.heads, sc.cands);
+  if (cudaGetLastError() != cudaSuccess) return D3S_ERR_CUDA;
+  return launch_wide<BF16>(a, 1, wide_kcap, st, 1 << 30, sc.heads, sc.cands);
+}
+
+template <bool BF16>
+int launch_fast1(const KArgs &a, const Scratch &sc, int nc, int wide_kcap, cudaStream_t st) {
+  switch (nc) {
+    case 17: return launch_fast1_nc<BF16, 17>(a, sc, wide_kcap, st);
+    case 25: return launch_fast1_nc<BF16, 25>(a, sc, wide_kcap, st);
+    case 33: return launch_fast1_nc<BF16, 33>(a, sc, wide_kcap, st);
+    default: return D3S_ERR_ARG;
+  }
+}
+
 // Small batches: one CTA per row runs the stats kernel's four warps and then,
 // in the same launch, the select work on warp 0; the wide kernel after it
 // (on at most N CTAs) takes any row handed on.
@@ -2016,9 +2404,9 @@ int launch_rowwarp(const KArgs &a, int nc, cudaStream_t st) {
   }
 }
 
-// Test hook: 0 = the usual choice, 1 = the stats + select pair, 3 = the
-// row-warp kernel, for batches that reach the choice between them (above the
-// small-batch path).
+// Test hook: 0 = the usual choice, 1 = the four-warp stats kernel + select,
+// 3 = the row-warp kernel, 4 = the one-warp stats kernel + select, for
+// batches that reach the choice between them (above the small-batch path).
 std::atomic<int> g_force_path{0};
 
 template <bool BF16>
@@ -2045,6 +2433,11 @@ int launch_typed(const KArgs &a, const Scratch &s, cudaStream_t st) {
     return launch_wide<BF16>(a, 1, scalar_k ? kscalar : D3S_MAX_K, st);
   }
   if (!s.heads || s.rec_capacity < a.N) return D3S_ERR_ARG;
+  // the stats pass by one warp per row for rows it holds (up to 33 chunks a
+  // lane); the four-warp stats kernel for longer rows, for per-row finite
+  // flags, and when path 1 is forced
+  if (force != 1 && !a.finite && nc >= 17)
+    return launch_fast1<BF16>(a, s, nc, scalar_k ? kscalar : D3S_MAX_K, st);
   return launch_fast<BF16>(a, s, J, scalar_k ? kscalar : D3S_MAX_K, st);
 }
 

@@ -16,8 +16,8 @@
 //     accumulator with tcgen05.ld, round to bf16 and store logits[b, v].
 //     When the tiles alone leave most SMs idle (small B) the K loop is split
 //     over the CTAs of a cluster, whose fp32 partials are added on chip
-//     through distributed shared memory. No multicast: every CTA loads its own
-//     tiles.
+//     through distributed shared memory. Every CTA loads its own tiles from
+//     this GPU's memory; no load is shared across the cluster.
 // Every wait on an mbarrier is bounded (kLmWaitLimitNs); a wait that gives up
 // sets the error word and the kernel drains its copies, frees its tensor
 // memory and returns.
@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // latency. The leader (rank 0) issues the MMAs; both CTAs' loads complete on
 // the leader's full barrier (mapa address); the leader commits each stage to
 // its own and to its peer's empty barrier, and the result to both accumulator
-// barriers (two plain commits: no multicast anywhere).
+// barriers (two plain commits, one per CTA).
 
 constexpr int kStages2 = 6;
 constexpr int kPairMinB = 512;  // from here the pair tiles alone fill the GPU (V = 4097: 136 CTAs at B = 1024)

@@ -251,7 +251,7 @@ def sample(logits: np.ndarray, temperature, top_k, top_p, seed) -> np.ndarray:
     return out
 
 
-PATH_AUTO, PATH_PAIR, PATH_ROWWARP = 0, 1, 3
+PATH_AUTO, PATH_PAIR, PATH_ROWWARP, PATH_PAIR1W = 0, 1, 3, 4
 
 
 def force_path(path: int) -> None:

@@ -163,8 +163,9 @@ D3S_API int d3s_debug_math(d3s_ctx *ctx, int op, const float *x_dev, float *y_de
                            float param, void *stream);
 /* Test hook (no counterpart in the reference): which kernel samples the
  * batches above the small-batch path (N > 512), process-wide: 0 = the usual
- * choice, 1 = the streaming stats kernel + the select kernel, 3 = the
- * row-warp kernel (one warp per row). A path that cannot take the request
+ * choice, 1 = the four-warp streaming stats kernel + the select kernel, 3 =
+ * the row-warp kernel (one warp per row), 4 = the one-warp streaming stats
+ * kernel + the select kernel. A path that cannot take the request
  * falls back to the usual one. Results are identical on every path; tests use
  * it to check each of them. */
 D3S_API int d3s_debug_force_path(int path);

@@ -1,7 +1,8 @@
 """Every kernel path that samples batches above the small-batch path (the
-streaming stats + select pair, the row-warp kernel of one warp per row)
-against the oracle on the same rows: forced in turn through
-the d3s_debug_force_path test hook. Ids, kept counts, statuses and the bits of
+four-warp streaming stats kernel with the select kernel, the row-warp kernel
+of one warp per row, the one-warp streaming stats kernel with the select
+kernel) against the oracle on the same rows: forced in turn through the
+d3s_debug_force_path test hook. Ids, kept counts, statuses and the bits of
 the race probabilities must be identical on every path."""
 
 import numpy as np
@@ -11,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-PATHS = [("pair", 1), ("rowwarp", 3)]
+PATHS = [("pair", 1), ("rowwarp", 3), ("pair1w", 4)]
 
 
 @pytest.fixture(scope="module")

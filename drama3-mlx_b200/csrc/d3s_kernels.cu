@@ -225,8 +225,66 @@ __device__ __forceinline__ float warp_rth_largest(float (&v)[M], int r) {
   }
 }
 
-// The serial end of a row, run by one warp: sorted[k] holds the top-k keys in
-// rank order, scr (>= 2 k + 8 floats, 16-byte aligned) is scratch, key draws
+// How the tail reads the ranked candidates. Ranks64: the top k as 64-bit
+// (value, id) keys. Ranks32: the top k as 32-bit value keys (okey of q) in
+// rank order; the id of a rank is looked up among the row's candidates by the
+// whole warp (ties in value keep their ids in increasing order, so the rank
+// r that is the m-th of the ranks holding its key is the m-th smallest id of the
+// candidates with that key).
+struct Ranks64 {
+  static constexpr bool kPerRankIds = true;
+  const unsigned long long *s;
+  __device__ __forceinline__ float value(int r) const { return cand_value(s[r]); }
+  __device__ __forceinline__ int32_t id(int r, int) const { return cand_id(s[r]); }
+};
+
+struct Ranks32 {
+  static constexpr bool kPerRankIds = false;
+  const uint32_t *s;                // top k, rank order
+  const uint32_t *keys;             // every candidate's key, list order
+  int C;
+  const unsigned long long *cs;     // raw candidates: the first kStageCands
+  const unsigned long long *slab;   // all of them
+  int staged;                       // how many cs holds
+  __device__ __forceinline__ float value(int r) const { return okey_to_float(s[r]); }
+  // called by every lane of the warp
+  __device__ __forceinline__ int32_t id(int r, int lane) const {
+    const uint32_t K = s[r];
+    int m = 0;  // ranks before r with the same key (they sit just before it)
+    for (int b = 0; b < r; b += 32) {
+      const int q = b + lane;
+      m += __popc(__ballot_sync(kFull, q < r && s[q] == K));
+    }
+    unsigned total = 0u;
+    int first = -1;
+    for (int b = 0; b < C; b += 32) {
+      const int e = b + lane;
+      const unsigned bal = __ballot_sync(kFull, e < C && keys[e] == K);
+      if (first < 0 && bal) first = b + __ffs(bal) - 1;
+      total += __popc(bal);
+    }
+    auto raw_id = [&](int e) {
+      return (uint32_t)(e < staged ? cs[e] : slab[e]);
+    };
+    if (total == 1u) return (int32_t)raw_id(first);
+    // ties: the m-th smallest id of the candidates with key K
+    uint32_t taken = 0u, id = 0u;
+    for (int t = 0; t <= m; ++t) {
+      uint32_t mine = 0xFFFFFFFFu;
+      for (int e = lane; e < C; e += 32)
+        if (keys[e] == K) {
+          const uint32_t v = raw_id(e);
+          if ((t == 0 || v > taken) && v < mine) mine = v;
+        }
+      id = __reduce_min_sync(kFull, mine);
+      taken = id;
+    }
+    return (int32_t)id;
+  }
+};
+
+// The serial end of a row, run by one warp: R gives the top k in rank order
+// (values and ids), scr (>= 2 k + 8 floats, 16-byte aligned) is scratch, key draws
 // the row's uniforms. Inclusive cumsum of exp(v - lse) in rank order
 // (src/sampling.c:39, :126-127), drop when cum > top_p at rank > 0 (:40-43,
 // :128), softmax over the survivors with a 1/sum multiply (:44, :129-134), race
@@ -244,9 +302,10 @@ __device__ __forceinline__ float warp_rth_largest(float (&v)[M], int r) {
 // it must stay at or below top_p under lse_lo plus that margin. Returns false,
 // having written nothing, when the cut cannot be certified; the caller then
 // computes the exact lse and calls again.
-__device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
-                                            const unsigned long long *sorted, float *scr, int k,
-                                            float lse_lo, float lse_hi, float top_p, int lane) {
+template <class Ranks>
+__device__ __forceinline__ bool sample_tail_r(const KArgs &a, int row, uint2 key, const Ranks &R,
+                                              float *scr, int k, float lse_lo, float lse_hi,
+                                              float top_p, int lane) {
   const bool exact = __float_as_uint(lse_lo) == __float_as_uint(lse_hi);
   // e_r = exp(v_r - lse), zero past k up to the next multiple of 4 (adding +0
   // leaves every running sum unchanged); under an interval, scr holds the terms
@@ -257,7 +316,7 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
   // the terms under lse_lo first (exact: the only terms); those under lse_hi
   // are needed only when the sum below leaves a cut possible
   for (int r = lane; r < k4; r += 32) {
-    const float e = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lse_lo)) : 0.0f;
+    const float e = r < k ? exp_full(__fsub_rn(R.value(r), lse_lo)) : 0.0f;
     scr_lo[r] = e;
     lsum = __fadd_rn(lsum, e);
   }
@@ -272,7 +331,7 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
   if (!(__fmul_rn(lsum, 1.0001f) <= top_p)) {
     if (!exact) {
       for (int r = lane; r < k4; r += 32)
-        scr[r] = r < k ? exp_full(__fsub_rn(cand_value(sorted[r]), lse_hi)) : 0.0f;
+        scr[r] = r < k ? exp_full(__fsub_rn(R.value(r), lse_hi)) : 0.0f;
       __syncwarp();
     }
     // cum_r = e_0 + ... + e_r in rank order; the first r > 0 with cum_r > top_p
@@ -307,10 +366,10 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
     }
   }
   __syncwarp();
-  const float top = cand_value(sorted[0]);
+  const float top = R.value(0);
   const int kept4 = (kept + 3) & ~3;
   for (int r = lane; r < kept4; r += 32)
-    scr[r] = r < kept ? exp_full(__fsub_rn(cand_value(sorted[r]), top)) : 0.0f;
+    scr[r] = r < kept ? exp_full(__fsub_rn(R.value(r), top)) : 0.0f;
   __syncwarp();
   float sum = 0.0f;
   for (int r0 = 0; r0 < kept; r0 += 4) {
@@ -344,15 +403,24 @@ __device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
   }
   if (a.probs)
     for (int r = kept + lane; r < k; r += 32) a.probs[(int64_t)row * a.ld_out + r] = 0.0f;
-  if (a.topk_ids)
-    for (int r = lane; r < k; r += 32) a.topk_ids[(int64_t)row * a.ld_out + r] = cand_id(sorted[r]);
+  if constexpr (Ranks::kPerRankIds) {
+    if (a.topk_ids)
+      for (int r = lane; r < k; r += 32) a.topk_ids[(int64_t)row * a.ld_out + r] = R.id(r, lane);
+  }
   const unsigned choice = __reduce_min_sync(kFull, best == wbest ? (unsigned)best_r : 0xffffffffu);
+  const int32_t chosen = R.id((int)choice, lane);
   if (lane == 0) {
-    a.ids[row] = cand_id(sorted[choice]);
+    a.ids[row] = chosen;
     if (a.status) a.status[row] = D3S_ROW_OK;
     if (a.kept) a.kept[row] = kept;
   }
   return true;
+}
+
+__device__ __forceinline__ bool sample_tail(const KArgs &a, int row, uint2 key,
+                                            const unsigned long long *sorted, float *scr, int k,
+                                            float lse_lo, float lse_hi, float top_p, int lane) {
+  return sample_tail_r(a, row, key, Ranks64{sorted}, scr, k, lse_lo, lse_hi, top_p, lane);
 }
 
 // Sum over the warp of each lane's fixed-point total (< 2^55): three 21/21/22-bit
@@ -990,6 +1058,60 @@ __device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[S], int l
   }
 }
 
+// The same network on 32-bit keys (one shuffle and a min / max a step).
+__device__ __forceinline__ void inreg_exchange32(uint32_t &x, uint32_t &y, bool desc) {
+  const uint32_t hi = max(x, y), lo = min(x, y);
+  x = desc ? hi : lo;
+  y = desc ? lo : hi;
+}
+
+template <int S>
+__device__ __forceinline__ void warp_sort_desc32(uint32_t (&v)[S], int lane) {
+  constexpr int n = 32 * S;
+#pragma unroll
+  for (int size = 2; size <= n; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride < 32) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+          const uint32_t o = __shfl_xor_sync(kFull, v[s], stride);
+          const bool desc = ((lane + 32 * s) & size) == 0;
+          const bool keep_max = ((lane & stride) == 0) == desc;
+          v[s] = keep_max ? max(v[s], o) : min(v[s], o);
+        }
+      } else if constexpr (S >= 2) {
+        // partners in the same lane; above 32 the direction depends on s only
+        if (stride == 32) {
+#pragma unroll
+          for (int s = 0; s < S; s += 2) inreg_exchange32(v[s], v[s + 1], ((32 * s) & size) == 0);
+        } else if constexpr (S >= 4) {
+#pragma unroll
+          for (int s = 0; s < S; ++s)
+            if ((s & 2) == 0) inreg_exchange32(v[s], v[s + 2], ((32 * s) & size) == 0);
+        }
+      }
+    }
+  }
+}
+
+// The k largest of C <= 32 S 32-bit keys (keys[], shared memory) into top[0..k)
+// in rank order.
+template <int S>
+__device__ __forceinline__ void sort_keys32(const uint32_t *keys, int C, int k, uint32_t *top,
+                                            int lane) {
+  uint32_t v[S];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const int e = lane + 32 * s;
+    v[s] = e < C ? keys[e] : 0u;
+  }
+  warp_sort_desc32<S>(v, lane);
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+    if (lane + 32 * s < k) top[lane + 32 * s] = v[s];
+}
+
 // Sort the row's C <= 32 S candidates (the first kStageCands staged in cs, the
 // rest in the slab) with the warp and store the first k keys, in rank order,
 // into sk.
@@ -1162,6 +1284,24 @@ __device__ __forceinline__ bool select_row(const KArgs &a, int row, int C,
   if (C > kCandCap || C < rp.k) {
     if (lane == 0) defer_row(a, row);
     return true;
+  }
+  if (C <= 128 && !a.topk_ids) {
+    // rank the 32-bit value keys (okey(q)); the tail looks up the drawn rank's id
+    uint32_t *top = reinterpret_cast<uint32_t *>(sk);  // [0, k)
+    uint32_t *keys = top + kFastMaxK;                   // [0, C)
+    for (int e = lane; e < C; e += 32)
+      keys[e] = okey(__fdiv_rn(
+          __uint_as_float((uint32_t)((e < kStageCands ? cs[e] : Cs.cand[e]) >> 32)), rp.T));
+    __syncwarp();
+    if (C <= 32)
+      sort_keys32<1>(keys, C, rp.k, top, lane);
+    else if (C <= 64)
+      sort_keys32<2>(keys, C, rp.k, top, lane);
+    else
+      sort_keys32<4>(keys, C, rp.k, top, lane);
+    __syncwarp();
+    return sample_tail_r(a, row, key, Ranks32{top, keys, C, cs, Cs.cand, kStageCands}, scr, rp.k,
+                         lse_lo, lse_hi, rp.p, lane);
   }
   rank_cands_smem(cs, Cs, C, rp.k, rp.T, sk, lane);
   __syncwarp();

@@ -175,3 +175,29 @@ def test_masked_rows_with_fewer_finite_logits_than_k(ctx, oracle, path):
     got = ids.cpu().numpy()
     assert (got == want).all(), f"{path}: rows {np.flatnonzero(got != want)[:10]}"
     ctx.check()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_tied_top_values(ctx, oracle, path, dtype):
+    """Rows whose largest values repeat (the max at up to four ids, the next
+    values twice or three times): the drawn rank often falls in a group of equal
+    values, whose ranks go to increasing ids."""
+    rng = np.random.default_rng(61)
+    N, V = 2600, 4097
+    x, T, p, k, seeds = rows_batch(N, V, 61)
+    for r in range(N):
+        order = np.argsort(-x[r])
+        for t in range(int(rng.integers(1, 6))):
+            src = order[t]
+            dst = rng.choice(V, int(rng.integers(1, 4)), replace=False)
+            x[r, dst] = x[r, src]
+    T[::3] = 0.05  # sharp rows: the draw lands on the top values
+    xt = dev(x, torch.bfloat16 if dtype == "bf16" else torch.float32)
+    ids = torch.empty(N, dtype=torch.int32, device="cuda")
+    kept = torch.empty_like(ids)
+    ctx.sample_rows(xt, ids, temperature=dev(T), top_p=dev(p), top_k=dev(k), seeds=dev(seeds),
+                    kept=kept)
+    want = oracle.sample_rows(host(xt), T, p, k, seeds.astype(np.uint64))
+    got = ids.cpu().numpy()
+    assert (got == want).all(), f"{path}: rows {np.flatnonzero(got != want)[:10]}"
+    ctx.check()

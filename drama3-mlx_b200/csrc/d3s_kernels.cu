@@ -1095,21 +1095,57 @@ __device__ __forceinline__ void warp_sort_desc32(uint32_t (&v)[S], int lane) {
   }
 }
 
-// The k largest of C <= 32 S 32-bit keys (keys[], shared memory) into top[0..k)
-// in rank order.
-template <int S>
-__device__ __forceinline__ void sort_keys32(const uint32_t *keys, int C, int k, uint32_t *top,
-                                            int lane) {
-  uint32_t v[S];
+// Bitonic merge of a bitonic sequence of 32 keys (one a lane) into descending
+// order.
+__device__ __forceinline__ uint32_t merge32_desc(uint32_t v, int lane) {
 #pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const int e = lane + 32 * s;
-    v[s] = e < C ? keys[e] : 0u;
+  for (int stride = 16; stride > 0; stride >>= 1) {
+    const uint32_t o = __shfl_xor_sync(kFull, v, stride);
+    v = (lane & stride) == 0 ? max(v, o) : min(v, o);
   }
-  warp_sort_desc32<S>(v, lane);
-#pragma unroll
-  for (int s = 0; s < S; ++s)
-    if (lane + 32 * s < k) top[lane + 32 * s] = v[s];
+  return v;
+}
+
+// Two descending 32-key lists (one key a lane) into one descending 64-key list:
+// hi holds ranks 0-31, lo ranks 32-63 ([a | reversed b] is bitonic).
+__device__ __forceinline__ void merge64_desc(uint32_t a, uint32_t b, uint32_t &hi, uint32_t &lo,
+                                             int lane) {
+  const uint32_t br = __shfl_sync(kFull, b, 31 - lane);
+  hi = merge32_desc(max(a, br), lane);
+  lo = merge32_desc(min(a, br), lane);
+}
+
+// The k largest of C <= 128 32-bit keys (keys[], shared memory, left as they
+// are) into top[0..k) in rank order, for k <= 64 or C <= 64: each 32-key block
+// sorted by the one-register network (a rolled loop, so one copy of its code),
+// pairs of blocks merged into sorted 64-key lists, and for more than 64 keys
+// the top 64 of two such lists (the elementwise max of one and the other
+// reversed is a bitonic sequence holding them) merged once more. top needs 128
+// entries.
+__device__ __forceinline__ void rank_keys32(const uint32_t *keys, int C, int k, uint32_t *top,
+                                            int lane) {
+  const int nb = (C + 31) >> 5;
+#pragma unroll 1
+  for (int b = 0; b < nb; ++b) {
+    uint32_t v[1] = {32 * b + lane < C ? keys[32 * b + lane] : 0u};
+    warp_sort_desc32<1>(v, lane);
+    top[32 * b + lane] = v[0];
+  }
+  __syncwarp();
+  if (nb == 1) return;  // the sorted block is the ranking
+  uint32_t p0, p1;
+  merge64_desc(top[lane], top[32 + lane], p0, p1, lane);
+  if (nb > 2) {
+    uint32_t q0, q1;
+    merge64_desc(top[64 + lane], nb > 3 ? top[96 + lane] : 0u, q0, q1, lane);
+    const uint32_t m0 = max(p0, __shfl_sync(kFull, q1, 31 - lane));
+    const uint32_t m1 = max(p1, __shfl_sync(kFull, q0, 31 - lane));
+    p0 = merge32_desc(max(m0, m1), lane);
+    p1 = merge32_desc(min(m0, m1), lane);
+  }
+  __syncwarp();
+  top[lane] = p0;
+  if (32 + lane < k) top[32 + lane] = p1;
 }
 
 // Sort the row's C <= 32 S candidates (the first kStageCands staged in cs, the
@@ -1285,20 +1321,15 @@ __device__ __forceinline__ bool select_row(const KArgs &a, int row, int C,
     if (lane == 0) defer_row(a, row);
     return true;
   }
-  if (C <= 128 && !a.topk_ids) {
+  if (C <= 128 && (rp.k <= 64 || C <= 64) && !a.topk_ids) {
     // rank the 32-bit value keys (okey(q)); the tail looks up the drawn rank's id
-    uint32_t *top = reinterpret_cast<uint32_t *>(sk);  // [0, k)
+    uint32_t *top = reinterpret_cast<uint32_t *>(sk);  // [0, 128)
     uint32_t *keys = top + kFastMaxK;                   // [0, C)
     for (int e = lane; e < C; e += 32)
       keys[e] = okey(__fdiv_rn(
           __uint_as_float((uint32_t)((e < kStageCands ? cs[e] : Cs.cand[e]) >> 32)), rp.T));
     __syncwarp();
-    if (C <= 32)
-      sort_keys32<1>(keys, C, rp.k, top, lane);
-    else if (C <= 64)
-      sort_keys32<2>(keys, C, rp.k, top, lane);
-    else
-      sort_keys32<4>(keys, C, rp.k, top, lane);
+    rank_keys32(keys, C, rp.k, top, lane);
     __syncwarp();
     return sample_tail_r(a, row, key, Ranks32{top, keys, C, cs, Cs.cand, kStageCands}, scr, rp.k,
                          lse_lo, lse_hi, rp.p, lane);

@@ -722,8 +722,8 @@ def run_ours(args):
                        "l2": "inputs 1.07 GB per GPU > 126 MB L2 (no flush needed)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "one sampler call: sample_stats_kernel<17,f32> + "
-                                   "sample_select_kernel + sample_wide_kernel (empty hand-off)",
+                         "kernel": "one sampler call: sample_stats1_kernel<33,f32> + "
+                                   "sample_select_kernel + sample_wide_kernel (the hand-off list)",
                          "kernel_ms": kernel_ms, "kernel_ms_max_over_ranks": kernel_ms_max,
                          "bytes_per_launch": bytes_per_launch},
             "per_rank_ms": [{"rank": r, "step_loop": v[0], "sample_mean": v[1],

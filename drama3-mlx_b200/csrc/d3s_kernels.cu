@@ -1871,6 +1871,164 @@ constexpr int kS1MaxWarps = 16;
 constexpr int kS1MaxDepth = 4;
 constexpr int kS1SmemBytes = 227 * 1024 - 1024;  // dynamic shared memory of the one-warp kernel's CTA
 
+// One row of the one-warp stats (the stage holds the row's bulk copy): the
+// bytes outside the row set to -inf, pass 1, the threshold, pass 2 (or the
+// exact stats), the candidates into the row's list and the header. cand_n is the
+// warp's candidate counter in shared memory (zero between rows).
+template <int NC, bool BF16>
+__device__ __forceinline__ void stats1_row(const KArgs &a, RowHead *heads, RowCands *cands,
+                                           unsigned char *stage, unsigned *cand_n, int row, int pst,
+                                           RowP rp, float c, float rT, int lane) {
+  constexpr int ESZ = BF16 ? 2 : 4;
+  constexpr int EPC = 16 / ESZ;
+  const int V = a.V;
+  const uintptr_t start =
+      (uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ;
+  const int s = (int)((start & 15) / ESZ);
+  const int nch = (int)((((start + (uintptr_t)V * ESZ + 15) & ~(uintptr_t)15) - (start & ~(uintptr_t)15)) / 16);
+  // -inf outside the row: the s elements before it, the rest of its last
+  // chunk, and every chunk past the copy up to the end of the stage
+  if constexpr (BF16) {
+    unsigned short *e = reinterpret_cast<unsigned short *>(stage);
+    if (lane < s) e[lane] = 0xFF80u;
+    if (V + s + lane < nch * EPC && lane < EPC) e[V + s + lane] = 0xFF80u;
+  } else {
+    float *e = reinterpret_cast<float *>(stage);
+    if (lane < s) e[lane] = -f_inf();
+    if (V + s + lane < nch * EPC && lane < EPC) e[V + s + lane] = -f_inf();
+  }
+  {
+    const uint4 ninf = BF16 ? make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u)
+                            : make_uint4(0xFF800000u, 0xFF800000u, 0xFF800000u, 0xFF800000u);
+    for (int ch = nch + lane; ch < 32 * NC; ch += 32) reinterpret_cast<uint4 *>(stage)[ch] = ninf;
+  }
+  __syncwarp();
+
+  // pass 1: chunk maxima, group maxima, the row max
+  float cm[NC];
+  float gm[4] = {-f_inf(), -f_inf(), -f_inf(), -f_inf()};
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    float x[EPC];
+    rw_chunk<BF16>(stage, lane + 32 * i, x);
+    float m = max_nan(x[0], x[1]);
+#pragma unroll
+    for (int e = 2; e < EPC; e += 2) m = max_nan(m, max_nan(x[e], x[e + 1]));
+    cm[i] = m;
+    gm[i & 3] = max_nan(gm[i & 3], m);
+  }
+  const float xmax = warp_max_nan(max_nan(max_nan(gm[0], gm[1]), max_nan(gm[2], gm[3])));
+
+  RowHead &H = heads[row];
+  // 0: written here (flagged or handed on), 1: approximate stats, 2: exact stats
+  int mode = 0;
+  float gmax = 0.0f, taux = 0.0f;
+  if (pst != D3S_ROW_OK) {
+    if (lane == 0) flag_row(a, row, pst);
+  } else if (rp.k > kFastMaxK) {
+    if (lane == 0) defer_row(a, row);
+  } else {
+    const float ax = fabsf(xmax);
+    gmax = (ax >= 0x1p-100f && ax <= 0x1p60f && rp.T >= 0x1p-17f && rp.T <= 0x1p20f)
+               ? div_rows(xmax, rT, -rp.T)
+               : __fdiv_rn(xmax, rp.T);  // max(x / T) = RN(max(x) / T): RN is monotone
+    if (!(fabsf(gmax) < f_inf())) {     // NaN, +inf, or every value -inf
+      if (lane == 0) flag_row(a, row, D3S_ROW_NONFINITE);
+    } else if (rp.k <= kApproxMaxK) {
+      const int r = (rp.k + 3) >> 2;  // <= 32
+      float v[4] = {gm[0], gm[1], gm[2], gm[3]}, t[4];
+      for (int j = 0;; ++j) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) t[g] = warp_max(v[g]);
+        if (j + 1 >= r) break;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) v[g] = v[g] == t[g] ? -f_inf() : v[g];
+      }
+      taux = fminf(fminf(t[0], t[1]), fminf(t[2], t[3]));
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        int n = 0;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) n += gm[h] >= t[g] ? 1 : 0;
+        if ((int)__reduce_add_sync(kFull, (unsigned)n) >= rp.k) taux = fmaxf(taux, t[g]);
+      }
+      mode = approx_row_ok(rp, xmax, taux) ? 1 : 2;
+    } else {
+      mode = 2;
+    }
+  }
+  if (mode == 0) {
+    if (lane == 0) H.done = 1;
+  } else {
+    RowCands &Cs = cands[row];
+    unsigned long long S;
+    if (mode == 1) {
+      // pass 2: the approximate full-row sum and the candidate chunks
+      const float tau_lo = __fmaf_rn(-fabsf(taux), 0x1p-21f, taux);
+      const float2 c2 = make_float2(c, c);
+      const float g = __fmul_rn(-xmax, c);
+      const float2 g2 = make_float2(g, g);
+      float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                       make_float2(0.0f, 0.0f)};
+      uint32_t b0 = 0u, b1 = 0u;  // bit i: chunk i (i < 32), chunk 32 + i
+#pragma unroll
+      for (int i = NC - 1; i >= 0; --i) {
+        float x[EPC];
+        rw_chunk<BF16>(stage, lane + 32 * i, x);
+#pragma unroll
+        for (int pp = 0; pp < EPC / 2; ++pp) {
+          const float2 u = __ffma2_rn(make_float2(x[2 * pp], x[2 * pp + 1]), c2, g2);
+          const int ai = (2 * i + pp) & 3;
+          acc[ai] = __fadd2_rn(acc[ai], make_float2(ex2_approx(u.x), ex2_approx(u.y)));
+        }
+        // the sign of tau_lo - max: set when the chunk holds an element > tau_lo
+        const uint32_t d = __float_as_uint(__fsub_rn(tau_lo, cm[i]));
+        if (i >= 32)
+          b1 = __funnelshift_l(d, b1, 1);
+        else
+          b0 = __funnelshift_l(d, b0, 1);
+      }
+      const float2 s4 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+      S = warp_sum_u64(__float2ull_rz(__fmul_rn(__fadd_rn(s4.x, s4.y), 0x1p46f)));
+      // the candidates of the marked chunks
+      while (__any_sync(kFull, (b0 | b1) != 0u)) {
+        if ((b0 | b1) != 0u) {
+          int i;
+          if (b0) {
+            i = __ffs(b0) - 1;
+            b0 &= b0 - 1;
+          } else {
+            i = 32 + __ffs(b1) - 1;
+            b1 &= b1 - 1;
+          }
+          const int ch = lane + 32 * i;
+          float x[EPC];
+          rw_chunk<BF16>(stage, ch, x);
+          int n = 0;
+#pragma unroll
+          for (int e = 0; e < EPC; ++e) n += x[e] > tau_lo ? 1 : 0;
+          unsigned pos = atomicAdd(cand_n, (unsigned)n);
+#pragma unroll
+          for (int e = 0; e < EPC; ++e)
+            if (x[e] > tau_lo) {
+              if (pos < (unsigned)kCandCap) Cs.cand[pos] = raw_cand(x[e], (uint32_t)(EPC * ch + e - s));
+              ++pos;
+            }
+        }
+      }
+    } else {
+      S = stats1_exact<NC, BF16>(a, rp, Cs, stage, cand_n, xmax, gmax, rT, s, lane);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      const int C = (int)atomicExch(cand_n, 0u);
+      reinterpret_cast<int4 *>(&H)[0] = make_int4(__float_as_int(gmax), 0, C, mode == 1 ? 1 : 0);
+      reinterpret_cast<ulonglong2 *>(&H)[1] = make_ulonglong2(S, 0ull);
+      reinterpret_cast<ulonglong2 *>(&H)[2] = make_ulonglong2(0ull, 0ull);
+    }
+  }
+}
+
 template <int NC, bool BF16>
 __global__ void __launch_bounds__(32 * kS1MaxWarps)
     sample_stats1_kernel(const KArgs a, RowHead *heads, RowCands *cands, int depth) {
@@ -1929,151 +2087,7 @@ __global__ void __launch_bounds__(32 * kS1MaxWarps)
       failed = true;
       break;
     }
-    const uintptr_t start =
-        (uintptr_t)a.logits + (uintptr_t)phys_row(a, row) * (uintptr_t)a.ld * ESZ;
-    const int s = (int)((start & 15) / ESZ);
-    const int nch = (int)((((start + (uintptr_t)V * ESZ + 15) & ~(uintptr_t)15) - (start & ~(uintptr_t)15)) / 16);
-    // -inf outside the row: the s elements before it, the rest of its last
-    // chunk, and every chunk past the copy up to the end of the stage
-    if constexpr (BF16) {
-      unsigned short *e = reinterpret_cast<unsigned short *>(stage);
-      if (lane < s) e[lane] = 0xFF80u;
-      if (V + s + lane < nch * EPC && lane < EPC) e[V + s + lane] = 0xFF80u;
-    } else {
-      float *e = reinterpret_cast<float *>(stage);
-      if (lane < s) e[lane] = -f_inf();
-      if (V + s + lane < nch * EPC && lane < EPC) e[V + s + lane] = -f_inf();
-    }
-    {
-      const uint4 ninf = BF16 ? make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u)
-                              : make_uint4(0xFF800000u, 0xFF800000u, 0xFF800000u, 0xFF800000u);
-      for (int ch = nch + lane; ch < 32 * NC; ch += 32) reinterpret_cast<uint4 *>(stage)[ch] = ninf;
-    }
-    __syncwarp();
-
-    // pass 1: chunk maxima, group maxima, the row max
-    float cm[NC];
-    float gm[4] = {-f_inf(), -f_inf(), -f_inf(), -f_inf()};
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      float x[EPC];
-      rw_chunk<BF16>(stage, lane + 32 * i, x);
-      float m = max_nan(x[0], x[1]);
-#pragma unroll
-      for (int e = 2; e < EPC; e += 2) m = max_nan(m, max_nan(x[e], x[e + 1]));
-      cm[i] = m;
-      gm[i & 3] = max_nan(gm[i & 3], m);
-    }
-    const float xmax = warp_max_nan(max_nan(max_nan(gm[0], gm[1]), max_nan(gm[2], gm[3])));
-
-    RowHead &H = heads[row];
-    // 0: written here (flagged or handed on), 1: approximate stats, 2: exact stats
-    int mode = 0;
-    float gmax = 0.0f, taux = 0.0f;
-    if (pst != D3S_ROW_OK) {
-      if (lane == 0) flag_row(a, row, pst);
-    } else if (rp.k > kFastMaxK) {
-      if (lane == 0) defer_row(a, row);
-    } else {
-      const float ax = fabsf(xmax);
-      gmax = (ax >= 0x1p-100f && ax <= 0x1p60f && rp.T >= 0x1p-17f && rp.T <= 0x1p20f)
-                 ? div_rows(xmax, rT, -rp.T)
-                 : __fdiv_rn(xmax, rp.T);  // max(x / T) = RN(max(x) / T): RN is monotone
-      if (!(fabsf(gmax) < f_inf())) {     // NaN, +inf, or every value -inf
-        if (lane == 0) flag_row(a, row, D3S_ROW_NONFINITE);
-      } else if (rp.k <= kApproxMaxK) {
-        const int r = (rp.k + 3) >> 2;  // <= 32
-        float v[4] = {gm[0], gm[1], gm[2], gm[3]}, t[4];
-        for (int j = 0;; ++j) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) t[g] = warp_max(v[g]);
-          if (j + 1 >= r) break;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) v[g] = v[g] == t[g] ? -f_inf() : v[g];
-        }
-        taux = fminf(fminf(t[0], t[1]), fminf(t[2], t[3]));
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          int n = 0;
-#pragma unroll
-          for (int h = 0; h < 4; ++h) n += gm[h] >= t[g] ? 1 : 0;
-          if ((int)__reduce_add_sync(kFull, (unsigned)n) >= rp.k) taux = fmaxf(taux, t[g]);
-        }
-        mode = approx_row_ok(rp, xmax, taux) ? 1 : 2;
-      } else {
-        mode = 2;
-      }
-    }
-    if (mode == 0) {
-      if (lane == 0) H.done = 1;
-    } else {
-      RowCands &Cs = cands[row];
-      unsigned long long S;
-      if (mode == 1) {
-        // pass 2: the approximate full-row sum and the candidate chunks
-        const float tau_lo = __fmaf_rn(-fabsf(taux), 0x1p-21f, taux);
-        const float2 c2 = make_float2(c, c);
-        const float g = __fmul_rn(-xmax, c);
-        const float2 g2 = make_float2(g, g);
-        float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
-                         make_float2(0.0f, 0.0f)};
-        uint32_t b0 = 0u, b1 = 0u;  // bit i: chunk i (i < 32), chunk 32 + i
-#pragma unroll
-        for (int i = NC - 1; i >= 0; --i) {
-          float x[EPC];
-          rw_chunk<BF16>(stage, lane + 32 * i, x);
-#pragma unroll
-          for (int pp = 0; pp < EPC / 2; ++pp) {
-            const float2 u = __ffma2_rn(make_float2(x[2 * pp], x[2 * pp + 1]), c2, g2);
-            const int ai = (2 * i + pp) & 3;
-            acc[ai] = __fadd2_rn(acc[ai], make_float2(ex2_approx(u.x), ex2_approx(u.y)));
-          }
-          // the sign of tau_lo - max: set when the chunk holds an element > tau_lo
-          const uint32_t d = __float_as_uint(__fsub_rn(tau_lo, cm[i]));
-          if (i >= 32)
-            b1 = __funnelshift_l(d, b1, 1);
-          else
-            b0 = __funnelshift_l(d, b0, 1);
-        }
-        const float2 s4 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
-        S = warp_sum_u64(__float2ull_rz(__fmul_rn(__fadd_rn(s4.x, s4.y), 0x1p46f)));
-        // the candidates of the marked chunks
-        while (__any_sync(kFull, (b0 | b1) != 0u)) {
-          if ((b0 | b1) != 0u) {
-            int i;
-            if (b0) {
-              i = __ffs(b0) - 1;
-              b0 &= b0 - 1;
-            } else {
-              i = 32 + __ffs(b1) - 1;
-              b1 &= b1 - 1;
-            }
-            const int ch = lane + 32 * i;
-            float x[EPC];
-            rw_chunk<BF16>(stage, ch, x);
-            int n = 0;
-#pragma unroll
-            for (int e = 0; e < EPC; ++e) n += x[e] > tau_lo ? 1 : 0;
-            unsigned pos = atomicAdd(&cand_n[w], (unsigned)n);
-#pragma unroll
-            for (int e = 0; e < EPC; ++e)
-              if (x[e] > tau_lo) {
-                if (pos < (unsigned)kCandCap) Cs.cand[pos] = raw_cand(x[e], (uint32_t)(EPC * ch + e - s));
-                ++pos;
-              }
-          }
-        }
-      } else {
-        S = stats1_exact<NC, BF16>(a, rp, Cs, stage, &cand_n[w], xmax, gmax, rT, s, lane);
-      }
-      __syncwarp();
-      if (lane == 0) {
-        const int C = (int)atomicExch(&cand_n[w], 0u);
-        reinterpret_cast<int4 *>(&H)[0] = make_int4(__float_as_int(gmax), 0, C, mode == 1 ? 1 : 0);
-        reinterpret_cast<ulonglong2 *>(&H)[1] = make_ulonglong2(S, 0ull);
-        reinterpret_cast<ulonglong2 *>(&H)[2] = make_ulonglong2(0ull, 0ull);
-      }
-    }
+    stats1_row<NC, BF16>(a, heads, cands, stage, &cand_n[w], row, pst, rp, c, rT, lane);
     // the stage has been read: the copy of row it + depth goes into it
     fence_proxy_async();
     __syncwarp();

@@ -1339,6 +1339,64 @@ __device__ __forceinline__ bool select_row(const KArgs &a, int row, int C,
   return sample_tail(a, row, key, sk, scr, rp.k, lse_lo, lse_hi, rp.p, lane);
 }
 
+// The rows whose cut needed the exact full-row sum, by the whole CTA once its
+// warps are done: thread t < 256 computes partial t of the definition, then warp
+// 0 ranks the row's stored candidates (sk: 256 keys of shared memory) and runs the
+// tail with the exact lse. Few rows per launch come here (the cut must fall
+// within about 1e-5 of top_p); doing them last keeps their reads of the row (long
+// evicted from L2) off every warp's critical path but one. Called by every thread
+// of the CTA (at least kPartials of them).
+__device__ __forceinline__ void finish_exact_rows(const KArgs &a, const RowHead *heads,
+                                                  const RowCands *cands, const int *rows, unsigned n,
+                                                  unsigned long long *red, unsigned long long *sk,
+                                                  float *scr) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  for (unsigned e = 0; e < n; ++e) {
+    const int xrow = rows[e];
+    RowP rp;
+    row_params(a, xrow, rp);
+    const RowHead &H = heads[xrow];
+    const float gmax = H.gmax;
+    if (t < kPartials) {
+      const int64_t off = phys_row(a, xrow) * a.ld;
+      const bool bf16 = a.dtype == D3S_BF16;
+      const float rT = __frcp_rn(rp.T), mT = -rp.T;
+      const bool recip = rp.T >= 0x1p-17f && rp.T <= 0x1p20f;  // div_rows' exact range of T
+      float xv[kFastMaxV / kPartials];
+#pragma unroll
+      for (int j = 0; j < kFastMaxV / kPartials; ++j) {
+        const int i = t + kPartials * j;
+        xv[j] = i < a.V ? (bf16 ? load_x<true>(a.logits, off + i) : load_x<false>(a.logits, off + i))
+                        : 0.0f;
+      }
+      float sp = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kFastMaxV / kPartials; ++j) {
+        if (t + kPartials * j < a.V) {
+          const float ax = fabsf(xv[j]);
+          const float q = (recip && ax >= 0x1p-100f && ax <= 0x1p60f) ? div_rows(xv[j], rT, mT)
+                                                                       : __fdiv_rn(xv[j], rp.T);
+          sp = __fadd_rn(sp, exp_term(__fsub_rn(q, gmax)));
+        }
+      }
+      const unsigned long long ws = warp_sum_fixed(__float2ull_rz(__fmul_rn(sp, 0x1p46f)));
+      if (lane == 0) red[w] = ws;
+    }
+    __syncthreads();
+    if (w == 0) {
+      unsigned long long Se = 0;
+#pragma unroll
+      for (int i = 0; i < kPartials / 32; ++i) Se += red[i];
+      const float lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
+      const RowCands &Cs = cands[xrow];
+      rank_cands_smem(Cs.cand, Cs, H.cnt, rp.k, rp.T, sk, lane);
+      __syncwarp();
+      sample_tail(a, xrow, row_key(a, xrow), sk, scr, rp.k, lse, lse, rp.p, lane);
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KArgs a,
                                                                         const RowHead *heads,
                                                                         const RowCands *cands) {
@@ -1412,57 +1470,10 @@ __global__ void __launch_bounds__(kSelThreads, 4) sample_select_kernel(const KAr
     }
     cnt_next = cnt_nn;
   }
-  // The rows whose cut needed the exact full-row sum, by the whole CTA once its
-  // warps are done: thread t computes partial t (256 threads, 256 partials) of
-  // the oracle's definition, then warp 0 ranks the row's stored candidates and
-  // runs the tail with the exact lse. Few rows per launch come here (the cut
-  // must fall within about 1e-5 of top_p); doing them last keeps their reads of
-  // the row (long evicted from L2) off every warp's critical path but one.
-  static_assert(kSelThreads == kPartials, "one partial per thread");
+  static_assert(kSelThreads >= kPartials, "one partial per thread");
   __syncthreads();
-  const unsigned n_exact = min(exact_n, (unsigned)kSelExactRows);
-  for (unsigned e = 0; e < n_exact; ++e) {
-    const int xrow = exact_rows[e];
-    RowP rp;
-    row_params(a, xrow, rp);
-    const RowHead &H = heads[xrow];
-    const float gmax = H.gmax;
-    const int64_t off = phys_row(a, xrow) * a.ld;
-    const bool bf16 = a.dtype == D3S_BF16;
-    const float rT = __frcp_rn(rp.T), mT = -rp.T;
-    const bool recip = rp.T >= 0x1p-17f && rp.T <= 0x1p20f;  // div_rows' exact range of T
-    float xv[kFastMaxV / kPartials];
-#pragma unroll
-    for (int j = 0; j < kFastMaxV / kPartials; ++j) {
-      const int i = threadIdx.x + kPartials * j;
-      xv[j] = i < a.V ? (bf16 ? load_x<true>(a.logits, off + i) : load_x<false>(a.logits, off + i))
-                      : 0.0f;
-    }
-    float sp = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kFastMaxV / kPartials; ++j) {
-      if ((int)threadIdx.x + kPartials * j < a.V) {
-        const float ax = fabsf(xv[j]);
-        const float q = (recip && ax >= 0x1p-100f && ax <= 0x1p60f) ? div_rows(xv[j], rT, mT)
-                                                                     : __fdiv_rn(xv[j], rp.T);
-        sp = __fadd_rn(sp, exp_term(__fsub_rn(q, gmax)));
-      }
-    }
-    const unsigned long long ws = warp_sum_fixed(__float2ull_rz(__fmul_rn(sp, 0x1p46f)));
-    if (lane == 0) exact_red[w] = ws;
-    __syncthreads();
-    if (w == 0) {
-      unsigned long long Se = 0;
-#pragma unroll
-      for (int i = 0; i < kSelWarps; ++i) Se += exact_red[i];
-      const float lse = __fadd_rn(gmax, log_full(__fmul_rn(__ull2float_rn(Se), 0x1p-46f)));
-      const RowCands &Cs = cands[xrow];
-      rank_cands_smem(Cs.cand, Cs, H.cnt, rp.k, rp.T, sk, lane);
-      __syncwarp();
-      sample_tail(a, xrow, row_key(a, xrow), sk, scr_all[0], rp.k, lse, lse, rp.p, lane);
-    }
-    __syncthreads();
-  }
+  finish_exact_rows(a, heads, cands, exact_rows, min(exact_n, (unsigned)kSelExactRows), exact_red,
+                    sk_all[0], scr_all[0]);
 }
 
 // ---- row-warp kernel: one warp takes a row from its logits to its draw ----

@@ -374,17 +374,34 @@ def measure_c2(ctx, torch, iters: int = 1000):
     torch.cuda.synchronize()
     per = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
     total_ms = a0.elapsed_time(b0)
+    # one call on each of the 64 batches captured once and replayed: the GPU
+    # time of a batch with no host submission in between
+    gs = torch.cuda.Stream()
+    gs.wait_stream(st)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(gs):
+        with torch.cuda.graph(graph, stream=gs):
+            for i in range(64):
+                ctx.sample_rows(xs[i], ids, temperature=0.7, top_p=0.7, top_k=30, seeds=seeds,
+                                stream=gs)
+    torch.cuda.synchronize()
+    reps = max(1, iters // 64)
+    graph_us = _events_ms(torch, graph.replay, reps) * 1e3 / 64
+    del graph
     peak, kind = load_peaks()
     bytes_batch = N * (2 * V + 8 + 4)
     p50 = per[len(per) // 2]
     ctx.check()
     return {"rows_per_s": N * iters / (total_ms / 1e3), "batch_p50_us": p50,
             "batch_p99_us": per[int(len(per) * 0.99)],
+            "graph_us_per_batch": graph_us, "rows_per_s_graph": N / (graph_us * 1e-6),
             "roofline": {"bound": "hbm", "achieved": bytes_batch / (p50 * 1e-6) / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": bytes_batch / (p50 * 1e-6) / 1e9 / peak,
                          "peak_source": kind, "bytes_per_batch": bytes_batch},
             "iterations": iters, "kernel": "one CTA per row, select in the same launch + wide (empty)",
-            "note": "a batch is 2.1 MB: latency-bound (launch + one row per CTA), far under HBM"}
+            "note": "a batch is 2.1 MB: latency-bound (launch + one row per CTA), far under HBM; "
+                    "rows_per_s and batch_p50 include the host's submission of each call, "
+                    "graph_us_per_batch is 64 calls replayed from one CUDA graph"}
 
 
 def measure_c3(ctx, torch, B: int, steps: int, warmup: int):

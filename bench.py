@@ -612,6 +612,17 @@ def run_ours(args):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
+    lines = [0]
+
+    def line_up():
+        """N > 1: every GPU's stream waits at a start line until all ranks'
+        streams reach it, so the timed work starts on all GPUs together (the
+        processes leave the barrier at different host times, and rank 0, which
+        waits for every rank's last step, would otherwise time that skew)."""
+        if gather is not None:
+            lines[0] += 1
+            gather.line_up(lines[0], stream=st)
+
     def over_ranks(vals: list[float]) -> list[list[float]]:
         if world == 1:
             return [vals]
@@ -632,6 +643,7 @@ def run_ours(args):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
     with Clocks(uuid, phys, 0.00025 if rank == 0 else 0.001) as clk:
+        line_up()
         start.record(st)
         for i in range(args.steps):
             out = target()
@@ -690,6 +702,7 @@ def run_ours(args):
         drain(hids if rank == 0 else None)
         barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        line_up()
         a.record(st)
         for _ in range(e2e_steps):
             e2e_step()

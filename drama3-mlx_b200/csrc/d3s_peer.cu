@@ -16,7 +16,7 @@
 // wait overlap the next step's sampling.
 //
 // Layout of the allocation rank 0 owns (exported by cudaIpcGetMemHandle):
-//   [0, 256)                      control words: arrived, released
+//   [0, 256)                      control words: arrived, released, lined_up
 //   [256, 256 + 4 N slots)        `slots` slots of N int32 ids
 #include <cstdio>
 #include <cstring>
@@ -44,6 +44,7 @@ constexpr unsigned long long kWaitNs = 5000000000ull;  // 5 s
 struct Ctrl {
   unsigned arrived;   // ranks' additions, cumulative over steps
   unsigned released;  // steps rank 0 has released (the next step it will gather)
+  unsigned lined_up;  // ranks' additions at start lines, cumulative
 };
 
 __device__ __forceinline__ unsigned long long now_ns() {
@@ -88,6 +89,25 @@ __global__ void gather_signal_kernel(unsigned *word) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   __threadfence_system();
   asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(word) : "memory");
+}
+
+// A start line: add 1 to *word (release, system scope, after every earlier
+// write of this stream), then wait (bounded by kWaitNs) until every rank's
+// addition for this line has landed (*word reaches target, acquire).
+__global__ void gather_line_kernel(unsigned *word, unsigned target, int32_t *err) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  __threadfence_system();
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(word) : "memory");
+  if ((int)(ld_acquire_sys(word) - target) >= 0) return;
+  const unsigned long long t0 = now_ns();
+  for (;;) {
+    __nanosleep(64);
+    if ((int)(ld_acquire_sys(word) - target) >= 0) return;
+    if (now_ns() - t0 > kWaitNs) {
+      atomicOr(err, 1);
+      return;
+    }
+  }
 }
 
 int gfail(int code, const char *msg) { return d3s::set_error(code, msg); }
@@ -223,6 +243,18 @@ int d3s_gather_release(d3s_gather *g, int64_t step, void *stream) {
                                                                         (unsigned)(step + 1));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return gcuda(e, "gather release launch");
+  return D3S_OK;
+}
+
+int d3s_gather_line_up(d3s_gather *g, int64_t line, void *stream) {
+  if (!g || line < 1) return gfail(D3S_ERR_ARG, "d3s_gather_line_up: bad argument");
+  if (!g->base) return gfail(D3S_ERR_ARG, "d3s_gather_line_up: not attached");
+  DevScope d(g->device);
+  const unsigned target = (unsigned)((uint64_t)g->world * (uint64_t)line);
+  gather_line_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(&ctrl(g)->lined_up, target,
+                                                                     g->error_local);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return gcuda(e, "gather start line launch");
   return D3S_OK;
 }
 

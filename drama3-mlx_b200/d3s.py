@@ -44,7 +44,7 @@ EXPORTS = ("d3s_version", "d3s_last_error", "d3s_key_from_seed", "d3s_key_split"
            "d3s_lmhead_sample", "d3s_codes_write_npy", "d3s_static_check",
            "d3s_static_debug_set_error", "d3s_gather_create", "d3s_gather_export",
            "d3s_gather_attach", "d3s_gather_begin", "d3s_gather_end", "d3s_gather_release",
-           "d3s_gather_check", "d3s_gather_destroy", "d3s_gather_copy_result",
+           "d3s_gather_check", "d3s_gather_destroy", "d3s_gather_copy_result", "d3s_gather_line_up",
            "d3s_debug_force_path")
 RAS_WINDOW = 16
 FRAME_EOS, FRAME_NONFINITE, FRAME_RETRY = 1, 2, 4
@@ -143,6 +143,7 @@ def lib() -> ctypes.CDLL:
         L.d3s_gather_release.argtypes = [vp, i64, vp]
         L.d3s_gather_check.argtypes = [vp, vp]
         L.d3s_gather_copy_result.argtypes = [vp, i64, vp, vp]
+        L.d3s_gather_line_up.argtypes = [vp, i64, vp]
         L.d3s_gather_destroy.argtypes = [vp]
         L.d3s_gather_destroy.restype = None
         L.d3s_static_debug_set_error.argtypes = [ctypes.c_int32, vp]
@@ -533,6 +534,11 @@ class Gather:
 
     def release(self, step: int, stream=None) -> None:
         _check(lib().d3s_gather_release(self._h, step, _stream_ptr(stream)))
+
+    def line_up(self, line: int, stream=None) -> None:
+        """d3s_gather_line_up: the stream waits until every rank's stream has
+        reached its line-th start line (line counts from 1 on every rank)."""
+        _check(lib().d3s_gather_line_up(self._h, line, _stream_ptr(stream)))
 
     def copy_result(self, step: int, out, stream=None):
         """Rank 0: the N ids of `step` into `out` (int32 CUDA tensor of N), on the stream."""

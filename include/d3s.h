@@ -250,6 +250,12 @@ D3S_API int d3s_gather_attach(d3s_gather *g, const void *handle);
 D3S_API int d3s_gather_begin(d3s_gather *g, int64_t step, int32_t **ids_dev, void *stream);
 D3S_API int d3s_gather_end(d3s_gather *g, int64_t step, int32_t **result_dev, void *stream);
 D3S_API int d3s_gather_release(d3s_gather *g, int64_t step, void *stream);
+/* A start line on `stream` (no counterpart in the reference: it lines up the
+ * ranks' GPUs, for timing): every rank's stream stops here until every rank's
+ * stream has reached its `line`-th start line (line = 1, 2, ... on every rank),
+ * so work queued after it starts on all GPUs together, whenever each host
+ * queued it. The wait gives up after 5 s and records it for d3s_gather_check. */
+D3S_API int d3s_gather_line_up(d3s_gather *g, int64_t line, void *stream);
 /* Rank 0: copy the N ids of `step` (after d3s_gather_end) to dst_dev, on `stream`. */
 D3S_API int d3s_gather_copy_result(d3s_gather *g, int64_t step, int32_t *dst_dev, void *stream);
 /* Waits for `stream`; D3S_ERR_CUDA (and clears it) when a wait of this rank

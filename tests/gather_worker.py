@@ -31,6 +31,7 @@ def main(out_dir: str, rows: int, steps: int) -> None:
         ids = torch.empty(rows, dtype=torch.int32, device="cuda")
         batches = [synth.c5_batch(rows, seed=300 + step, V=2049) for step in range(steps)]
         dist.barrier(device_ids=[local])
+        g.line_up(1)  # both GPUs start the steps together
         for step, (x, T, p, k, seeds) in enumerate(batches):
             ptr = g.begin(step)
             ctx.sample_rows(x[s:e], ptr, temperature=T[s:e], top_p=p[s:e], top_k=k[s:e],

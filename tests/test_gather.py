@@ -1,8 +1,9 @@
 """The gather of sampled ids to rank 0 over NVLink peer memory (d3s_gather):
 one rank (the result equals the sampler's own ids), a wait for a rank that
-never arrives (it gives up with an error the host reads, and the device stays
-usable), and two GPUs (each rank's sampler writes its shard into rank 0's
-result; every step equals the oracle), the last only where two GPUs exist."""
+never arrives, at a step's end or at a start line (it gives up with an error
+the host reads, and the device stays usable), and two GPUs (each rank's
+sampler writes its shard into rank 0's result; every step equals the oracle),
+the last only where two GPUs exist."""
 
 import os
 import socket
@@ -34,6 +35,8 @@ def test_gather_one_rank_equals_local_ids(d3s):
     g = d3s.Gather(0, 1, 0, 3000, lambda mine: mine)
     out = torch.empty(3000, dtype=torch.int32, device="cuda")
     want = torch.empty_like(out)
+    for line in (1, 2):  # one rank reaches every start line at once
+        g.line_up(line)
     for step in range(5):
         x, T, p, k, seeds = synth.c5_batch(3000, seed=40 + step)
         ctx.sample_rows(x, want, temperature=T, top_p=p, top_k=k, seeds=seeds)
@@ -65,6 +68,27 @@ def test_gather_wait_for_a_missing_rank_gives_up(d3s):
     assert e.value.code == d3s.D3S_ERR_CUDA
     assert time.time() - t0 < 30
     g.check()  # reported once, then cleared
+    ids = torch.empty(64, dtype=torch.int32, device="cuda")
+    ctx.sample_rows(x, ids, temperature=T, top_p=p, top_k=k, seeds=seeds)
+    ctx.check()
+    g.close()
+    ctx.close()
+
+
+def test_start_line_without_the_other_rank_gives_up(d3s):
+    """Rank 0 of a world of 2 at a start line its peer never reaches: the wait
+    runs out (5 s), the gather reports it once, and the device still works."""
+    import synth
+    g = d3s.Gather(0, 2, 0, 64, lambda mine: mine)
+    t0 = time.time()
+    g.line_up(1)
+    with pytest.raises(d3s.D3SError) as e:
+        g.check()
+    assert e.value.code == d3s.D3S_ERR_CUDA
+    assert time.time() - t0 < 30
+    g.check()
+    ctx = d3s.Context(0)
+    x, T, p, k, seeds = synth.c5_batch(64, seed=51)
     ids = torch.empty(64, dtype=torch.int32, device="cuda")
     ctx.sample_rows(x, ids, temperature=T, top_p=p, top_k=k, seeds=seeds)
     ctx.check()

@@ -134,6 +134,10 @@ class Clocks:
                     pass
                 self._stop.wait(self.interval_s)
 
+        # the main thread enqueues launches while holding the interpreter: switch
+        # threads often so the poller runs during the timed region
+        self._switch = sys.getswitchinterval()
+        sys.setswitchinterval(1e-4)
         self._thread = threading.Thread(target=poll, daemon=True)
         self._thread.start()
         return self
@@ -142,6 +146,7 @@ class Clocks:
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=5)
+            sys.setswitchinterval(self._switch)
 
     def summary(self):
         if self.err:
@@ -724,7 +729,17 @@ def run_ours(args):
     cpu = None
     latency = None
     configs = None
+    calibration = None
     if rank == 0 and world == 1:
+        # what a plain read of the same logits costs: torch's own reductions over
+        # the 1.07 GB, timed the same way (CUDA events, warm)
+        read_ms = min(_events_ms(torch, lambda: torch.sum(x, dtype=torch.float32), 10),
+                      _events_ms(torch, lambda: torch.amax(x, dim=1), 10))
+        calibration = {"torch_read_of_logits_ms": read_ms,
+                       "torch_read_GBs": x.numel() * x.element_size() / (read_ms * 1e-3) / 1e9,
+                       "sampler_call_vs_read": read_ms / kernel_ms,
+                       "note": "the faster of torch.sum and torch.amax(dim=1) over the logits: a "
+                               "plain read of the bytes the sampler's stream reads"}
         if not args.no_latency:
             latency = c1_latency(ctx, torch)
         if not args.no_configs:
@@ -763,6 +778,7 @@ def run_ours(args):
             "gpu_launches": (3 + (2 if world > 1 else 0)) * args.steps,
             "cpu_baseline": cpu,
             "latency": latency,
+            "calibration": calibration,
             "configs": configs,
         }
         print(json.dumps(line), flush=True)

@@ -284,7 +284,7 @@ struct Ranks32 {
 };
 
 // The serial end of a row, run by one warp: R gives the top k in rank order
-// (values and ids), scr (>= 2 k + 8 floats, 16-byte aligned) is scratch, key draws
+// (values and ids), scr (>= k + 4 floats, 16-byte aligned) is scratch, key draws
 // the row's uniforms. Inclusive cumsum of exp(v - lse) in rank order
 // (src/sampling.c:39, :126-127), drop when cum > top_p at rank > 0 (:40-43,
 // :128), softmax over the survivors with a 1/sum multiply (:44, :129-134), race
@@ -307,62 +307,66 @@ __device__ __forceinline__ bool sample_tail_r(const KArgs &a, int row, uint2 key
                                               float *scr, int k, float lse_lo, float lse_hi,
                                               float top_p, int lane) {
   const bool exact = __float_as_uint(lse_lo) == __float_as_uint(lse_hi);
-  // e_r = exp(v_r - lse), zero past k up to the next multiple of 4 (adding +0
-  // leaves every running sum unchanged); under an interval, scr holds the terms
-  // under lse_hi and scr_lo those under lse_lo
+  // e_r = exp(v_r - lse_hi) (exact: under the exact lse), zero past k up to the
+  // next multiple of 4 (adding +0 leaves every running sum unchanged)
   const int k4 = (k + 3) & ~3;
-  float *scr_lo = exact ? scr : scr + k4;
   float lsum = 0.0f;
-  // the terms under lse_lo first (exact: the only terms); those under lse_hi
-  // are needed only when the sum below leaves a cut possible
   for (int r = lane; r < k4; r += 32) {
-    const float e = r < k ? exp_full(__fsub_rn(R.value(r), lse_lo)) : 0.0f;
-    scr_lo[r] = e;
+    const float e = r < k ? exp_full(__fsub_rn(R.value(r), lse_hi)) : 0.0f;
+    scr[r] = e;
     lsum = __fadd_rn(lsum, e);
   }
-  // Any-order sum of the k terms: a sequential sum of nonnegative terms differs
-  // from it by at most 2 (k - 1) 2^-24 relative (< 3.1e-5 for k <= 256). When
-  // even that bound stays <= top_p, no prefix sum can exceed top_p: nothing is cut.
-  // (Under an interval the sum is of the terms under lse_lo, the largest.)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) lsum = __fadd_rn(lsum, __shfl_xor_sync(kFull, lsum, o));
   __syncwarp();
+  // Under an interval, a term under lse_lo is at most F times the same rank's
+  // term under lse_hi plus 0.75 2^-24: F covers exp(lse_hi - lse_lo) and exp's
+  // error at both ends; the arguments' roundings (|y| 2^-24 each, y = v - lse
+  // <= 0) move a term e^y by at most 2 |y| e^y 2^-24 <= (2 / e) 2^-24. A wide
+  // interval (above 2^-14) gets no bound: F = inf, and any cut it needs is left
+  // to the exact sum.
+  float F = 1.0f;
+  if (!exact) {
+    const float d = __fsub_ru(lse_hi, lse_lo);
+    F = d <= 0x1p-14f ? __fadd_ru(1.0f, __fadd_ru(__fmul_ru(d, 1.0001f), 0x1p-22f)) : f_inf();
+  }
+  // Any-order sum of the k terms: a sequential sum of nonnegative terms differs
+  // from it by at most 2 (k - 1) 2^-24 relative (< 3.1e-5 for k <= 256). When
+  // even that bound stays <= top_p, no prefix sum can exceed top_p: nothing is
+  // cut. (Under an interval, for the terms under lse_lo, the largest.)
+  const float lsum_lo = exact ? lsum : __fmaf_ru(F, lsum, (float)k * 0x1p-24f);
   int kept = k;
-  if (!(__fmul_rn(lsum, 1.0001f) <= top_p)) {
-    if (!exact) {
-      for (int r = lane; r < k4; r += 32)
-        scr[r] = r < k ? exp_full(__fsub_rn(R.value(r), lse_hi)) : 0.0f;
-      __syncwarp();
-    }
+  if (!(__fmul_ru(lsum_lo, 1.0001f) <= top_p)) {
     // cum_r = e_0 + ... + e_r in rank order; the first r > 0 with cum_r > top_p
-    // is the cut. Four ranks per step: the running sums, then one test.
-    // Under an interval the same running sums of the terms under lse_lo go
-    // alongside: before_lo is the sum of ranks 0 .. kept - 1 under lse_lo.
-    float cum = 0.0f, cut = 0.0f, cum_lo = 0.0f, before_lo = 0.0f;
+    // is the cut. Four ranks per step: the running sums, then one test. before
+    // is the sum of ranks 0 .. kept - 1 (all k when nothing is cut).
+    float cum = 0.0f, cut = 0.0f, before = 0.0f;
+    bool found = false;
     for (int r0 = 0; r0 < k; r0 += 4) {
       const float4 e4 = *reinterpret_cast<const float4 *>(scr + r0);
-      const float4 l4 = *reinterpret_cast<const float4 *>(scr_lo + r0);
       const float c0 = __fadd_rn(cum, e4.x), c1 = __fadd_rn(c0, e4.y);
       const float c2 = __fadd_rn(c1, e4.z), c3 = __fadd_rn(c2, e4.w);
-      const float l0 = __fadd_rn(cum_lo, l4.x), l1 = __fadd_rn(l0, l4.y);
-      const float l2 = __fadd_rn(l1, l4.z), l3 = __fadd_rn(l2, l4.w);
       const bool h0 = r0 > 0 && c0 > top_p;  // rank 0 is never dropped
       if (h0 || c1 > top_p || c2 > top_p || c3 > top_p) {
         kept = h0 ? r0 : (c1 > top_p ? r0 + 1 : (c2 > top_p ? r0 + 2 : r0 + 3));
         cut = h0 ? c0 : (c1 > top_p ? c1 : (c2 > top_p ? c2 : c3));
-        before_lo = h0 ? cum_lo : (c1 > top_p ? l0 : (c2 > top_p ? l1 : l2));
+        before = h0 ? cum : (c1 > top_p ? c0 : (c2 > top_p ? c1 : c2));
+        found = true;
         break;
       }
       cum = c3;
-      cum_lo = l3;
     }
+    if (!found) before = cum;
     if (!exact) {
       // margin: two sequential sums of <= kept + 1 terms (kept 2^-24 each),
       // exp's order error (2.9 2^-24 for its error below 2^-23.5) and the
-      // product's rounding
+      // product's rounding; the sum under lse_lo, bounded from the one under
+      // lse_hi, takes two more sequential-sum errors
       const float mu = __fmul_rn((float)(2 * kept + 6), 0x1p-24f);
       if (kept < k && !(__fmul_rn(cut, 1.0f - mu) > top_p)) return false;
-      if (kept >= 2 && !(__fmul_rn(kept < k ? before_lo : cum_lo, 1.0f + mu) <= top_p)) return false;
+      const float before_lo = __fmaf_ru(F, before, (float)kept * 0x1.8p-25f);
+      const float mu2 = __fmul_rn((float)(4 * kept + 8), 0x1p-24f);
+      if (kept >= 2 && !(__fmul_ru(before_lo, 1.0f + mu2) <= top_p)) return false;
     }
   }
   __syncwarp();

@@ -6,6 +6,7 @@
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
+#include <chrono>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -589,7 +590,7 @@ constexpr int kHandedOn = 1;
 static int d3_sample_row(d3s_ctx *ctx, const float *logits, int V, float temperature, int top_k,
                          float top_p, d3s_key sub, int *out) {
   const size_t lbytes = ((size_t)V * sizeof(float) + 15) & ~(size_t)15;
-  const size_t need = lbytes + 16;
+  const size_t need = lbytes + 16;  // the row, then id, status and the done word
   cudaError_t e;
   if (need > ctx->row_cap) {
     cudaStreamSynchronize(ctx->stream);  // the old buffer may be in use by queued work
@@ -610,6 +611,7 @@ static int d3_sample_row(d3s_ctx *ctx, const float *logits, int V, float tempera
   volatile int32_t *res = reinterpret_cast<volatile int32_t *>(ctx->row_host + lbytes);
   res[0] = INT32_MIN;  // stays when the row is handed on
   res[1] = D3S_ROW_OK;
+  res[2] = 0;          // the kernel sets it once the results are written
   d3s_request r{};
   r.logits = ctx->row_dev;
   r.dtype = D3S_F32;
@@ -626,10 +628,20 @@ static int d3_sample_row(d3s_ctx *ctx, const float *logits, int V, float tempera
   d3s::KArgs a = to_kargs(&r, ctx);
   a.direct = 1;        // the kernel loads the mapped row itself (no waits, no error word)
   a.skip_handoff = 1;  // a handed-on row is caught below
+  a.done_flag = r.ids + 2;
   if (d3s::launch_sample(a, ctx->scratch, ctx->stream) != D3S_OK)
     return cuda_fail(cudaGetLastError(), "sampler launch");
-  e = cudaStreamSynchronize(ctx->stream);
-  if (e != cudaSuccess) return cuda_fail(e, "d3_sample");
+  // Poll the done word the kernel writes last (the row was read long before, so
+  // the next call may refill the staging at once); after 1 s, or when the word
+  // never comes, the stream's own synchronisation decides (and reports errors).
+  const auto t0 = std::chrono::steady_clock::now();
+  for (unsigned spin = 0; res[2] == 0; ++spin)
+    if ((spin & 1023u) == 1023u && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(1))
+      break;
+  if (res[2] == 0) {
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "d3_sample");
+  }
   const int32_t id = res[0], st = res[1];
   if (id == INT32_MIN) return kHandedOn;
   out[0] = id;

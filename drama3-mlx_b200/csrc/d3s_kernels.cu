@@ -994,6 +994,15 @@ __global__ void __launch_bounds__(kFastThreads, kStatMinBlocks)
       }
     }
   }
+  if (SELECT && a.done_flag) {
+    // every result of the launch is written (thread 0 wrote the row's id and
+    // status itself): publish it to the host polling mapped memory
+    __syncthreads();
+    if (t == 0) {
+      __threadfence_system();
+      *reinterpret_cast<volatile int32_t *>(a.done_flag) = 1;
+    }
+  }
   if (failed) {
     // A bulk copy did not complete in time: record it, then wait (bounded) for
     // this CTA's copies still in flight before the shared memory goes away.

@@ -50,6 +50,10 @@ struct KArgs {
   // the row-independent part of the approximate full-row sum's relative error
   // bound (set by the launcher of the approximate-sum kernels)
   float approx_c0;
+  // zero-copy one-row calls: set to 1 (in mapped host memory) once every
+  // result of the launch is written, so the host can poll it instead of
+  // waiting for the stream
+  int32_t *done_flag;
 };
 
 // Per-row results the stats kernel passes to the select kernel. The header

@@ -80,6 +80,29 @@ __device__ __forceinline__ float exp_full(float x) {
   return __fmul_rn(__fmul_rn(p, s1), s2);
 }
 
+// exp_full for x <= 0 (the tail's terms: quotients never exceed the row max,
+// and lse is at least the max): the same arithmetic without the overflow test
+// and the upward scaling step, which cannot apply there.
+__device__ __forceinline__ float exp_nonpos(float x) {
+  if (x < -104.0f) return 0.0f;
+  float t = __fmaf_rn(x, kL2E, kShifter);
+  float nf = __fsub_rn(t, kShifter);
+  int n = (int)(__float_as_uint(t) - kShifterBits);
+  float r = __fmaf_rn(nf, -kLn2Hi, x);
+  r = __fmaf_rn(nf, -kLn2Lo, r);
+  float p = kE6;
+  p = __fmaf_rn(p, r, kE5);
+  p = __fmaf_rn(p, r, kE4);
+  p = __fmaf_rn(p, r, kE3);
+  p = __fmaf_rn(p, r, kE2);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int n2 = n < -126 ? -64 : 0;
+  float s1 = __uint_as_float((unsigned)(n - n2 + 127) << 23);
+  float s2 = __uint_as_float((unsigned)(n2 + 127) << 23);
+  return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
 // p * 2^n for p in [0.7, 1.42] and n >= -124, as integers: t = 1.5 * 2^23 + n has
 // bits 0x4B400000 + n, and (0x4B400000 << 23) wraps to 0, so bits(p) + (t's bits
 // << 23) adds n to p's exponent. The result is normal, so this is exactly the

@@ -312,7 +312,7 @@ __device__ __forceinline__ bool sample_tail_r(const KArgs &a, int row, uint2 key
   const int k4 = (k + 3) & ~3;
   float lsum = 0.0f;
   for (int r = lane; r < k4; r += 32) {
-    const float e = r < k ? exp_full(__fsub_rn(R.value(r), lse_hi)) : 0.0f;
+    const float e = r < k ? exp_nonpos(__fsub_rn(R.value(r), lse_hi)) : 0.0f;
     scr[r] = e;
     lsum = __fadd_rn(lsum, e);
   }
@@ -373,7 +373,7 @@ __device__ __forceinline__ bool sample_tail_r(const KArgs &a, int row, uint2 key
   const float top = R.value(0);
   const int kept4 = (kept + 3) & ~3;
   for (int r = lane; r < kept4; r += 32)
-    scr[r] = r < kept ? exp_full(__fsub_rn(R.value(r), top)) : 0.0f;
+    scr[r] = r < kept ? exp_nonpos(__fsub_rn(R.value(r), top)) : 0.0f;
   __syncwarp();
   float sum = 0.0f;
   for (int r0 = 0; r0 < kept; r0 += 4) {
